@@ -1,0 +1,217 @@
+// f32 fp_attention on FP32 FMA (CUDA cores).
+//
+// Same algorithm as the reference kernel (lib/Plan/TritonEmitter.cpp:73-104,
+// twin python/fusionpass/kernels.py:58-89): one CTA per (64 query rows,
+// batch*head), K/V streamed in 64-key tiles through shared memory, online
+// softmax with f32 running max m_i, sum l_i and accumulator acc, IEEE f32 dot
+// products, out-of-range keys at -inf, one division acc / l_i at the end.
+//
+// 256 threads as a 16 x 16 grid: thread (ty, tx) owns query rows 4*ty..4*ty+3,
+// score columns tx + 16*c and output columns tx + 16*c.  The 16 threads of a
+// row form one half-warp, so the row max / sum are half-warp shuffles.
+#include <atomic>
+#include <cmath>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace fpk {
+namespace attn32 {
+
+constexpr int kBM = 64;
+constexpr int kBN = 64;
+constexpr int kThreads = 256;
+
+struct Params {
+  const float* q;
+  const float* k;
+  const float* v;
+  float* o;
+  int64_t heads, seq, num_mtiles;
+  int64_t qs[3], ks[3], vs[3], os[3];  // b, h, s element strides
+  float scale;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) attn_f32_kernel(const __grid_constant__ Params p) {
+  constexpr int DC = D / 16;  // output columns per thread
+  extern __shared__ __align__(16) float smem_f[];
+  float(*Qs)[kBM] = reinterpret_cast<float(*)[kBM]>(smem_f);                          // Qs[d][row]
+  float(*Ks)[kBN + 1] = reinterpret_cast<float(*)[kBN + 1]>(smem_f + D * kBM);        // Ks[d][key]
+  float(*Vs)[D] = reinterpret_cast<float(*)[D]>(smem_f + D * kBM + D * (kBN + 1));   // Vs[key][d]
+  float(*Ps)[kBN + 1] = reinterpret_cast<float(*)[kBN + 1]>(smem_f + D * kBM + D * (kBN + 1) + kBN * D);
+
+  const int tid = threadIdx.x;
+  const int tx = tid & 15;
+  const int ty = tid >> 4;
+  const int64_t bh = blockIdx.x / p.num_mtiles;
+  const int64_t m0 = (blockIdx.x % p.num_mtiles) * kBM;
+  const int64_t b = bh / p.heads, h = bh % p.heads;
+  const float* qb = p.q + b * p.qs[0] + h * p.qs[1];
+  const float* kb = p.k + b * p.ks[0] + h * p.ks[1];
+  const float* vb = p.v + b * p.vs[0] + h * p.vs[1];
+  float* ob = p.o + b * p.os[0] + h * p.os[1];
+  const int64_t S = p.seq;
+
+  // Q tile -> Qs (rows past S read as 0, kernels.py:66-67)
+  for (int idx = tid; idx < kBM * D; idx += kThreads) {
+    const int r = idx % kBM, d = idx / kBM;
+    const int64_t gr = m0 + r;
+    Qs[d][r] = gr < S ? qb[gr * p.qs[2] + d] : 0.0f;
+  }
+
+  float m_i[4], l_i[4], acc[4][DC];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m_i[i] = -INFINITY;
+    l_i[i] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < DC; ++c) acc[i][c] = 0.0f;
+  }
+
+  for (int64_t n0 = 0; n0 < S; n0 += kBN) {
+    __syncthreads();  // previous tile fully consumed (and Qs written on the first pass)
+    for (int idx = tid; idx < kBN * D; idx += kThreads) {
+      const int j = idx / D, d = idx % D;
+      const int64_t gj = n0 + j;
+      const bool ok = gj < S;
+      Ks[d][j] = ok ? kb[gj * p.ks[2] + d] : 0.0f;
+      Vs[j][d] = ok ? vb[gj * p.vs[2] + d] : 0.0f;
+    }
+    __syncthreads();
+
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[i][c] = 0.0f;
+#pragma unroll 8
+    for (int d = 0; d < D; ++d) {
+      const float4 qv = *reinterpret_cast<const float4*>(&Qs[d][4 * ty]);
+      const float qa[4] = {qv.x, qv.y, qv.z, qv.w};
+      float kv[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) kv[c] = Ks[d][tx + 16 * c];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s[i][c] = fmaf(qa[i], kv[c], s[i][c]);
+    }
+
+    float alpha[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const bool ok = n0 + tx + 16 * c < S;
+        s[i][c] = ok ? s[i][c] * p.scale : -INFINITY;  // kernels.py:76-77
+        mx = fmaxf(mx, s[i][c]);
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_new = fmaxf(m_i[i], mx);
+      alpha[i] = expf(m_i[i] - m_new);
+      float rs = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float pv = expf(s[i][c] - m_new);
+        Ps[4 * ty + i][tx + 16 * c] = pv;
+        rs += pv;
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off);
+      l_i[i] = l_i[i] * alpha[i] + rs;
+      m_i[i] = m_new;
+    }
+    __syncthreads();
+
+    float pv_acc[4][DC];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < DC; ++c) pv_acc[i][c] = 0.0f;
+#pragma unroll 4
+    for (int j = 0; j < kBN; ++j) {
+      float pr[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pr[i] = Ps[4 * ty + i][j];
+#pragma unroll
+      for (int c = 0; c < DC; ++c) {
+        const float vv = Vs[j][tx + 16 * c];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pv_acc[i][c] = fmaf(pr[i], vv, pv_acc[i][c]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < DC; ++c) acc[i][c] = acc[i][c] * alpha[i] + pv_acc[i][c];
+  }
+
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t gr = m0 + 4 * ty + i;
+    if (gr >= S) continue;
+#pragma unroll
+    for (int c = 0; c < DC; ++c) ob[gr * p.os[2] + tx + 16 * c] = acc[i][c] / l_i[i];
+  }
+}
+
+template <int D>
+constexpr int smem_bytes() {
+  return static_cast<int>(sizeof(float)) * (D * kBM + D * (kBN + 1) + kBN * D + kBM * (kBN + 1));
+}
+
+template <int D>
+static int launch_d(const Params& p, int64_t blocks, cudaStream_t s) {
+  static std::atomic<int> opted[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FPK_ERR_CUDA;
+  if (!opted[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(attn_f32_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem_bytes<D>()) != cudaSuccess)
+      return FPK_ERR_CUDA;
+    opted[dev].store(1, std::memory_order_release);
+  }
+  attn_f32_kernel<D><<<static_cast<unsigned>(blocks), kThreads, smem_bytes<D>(), s>>>(p);
+  return cudaGetLastError() == cudaSuccess ? FPK_OK : FPK_ERR_CUDA;
+}
+
+}  // namespace attn32
+
+int launch_attention_f32(const fpk_attn_desc* d, const void* q, const void* k, const void* v, void* o,
+                         cudaStream_t stream, const DeviceInfo& dev) {
+  using namespace attn32;
+  (void)dev;
+  const uintptr_t ptrs[4] = {reinterpret_cast<uintptr_t>(q), reinterpret_cast<uintptr_t>(k),
+                             reinterpret_cast<uintptr_t>(v), reinterpret_cast<uintptr_t>(o)};
+  for (uintptr_t a : ptrs)
+    if (a % 4) return FPK_ERR_ALIGN;
+  Params p;
+  p.q = static_cast<const float*>(q);
+  p.k = static_cast<const float*>(k);
+  p.v = static_cast<const float*>(v);
+  p.o = static_cast<float*>(o);
+  p.heads = d->heads;
+  p.seq = d->seq_len;
+  p.num_mtiles = (d->seq_len + kBM - 1) / kBM;
+  for (int i = 0; i < 3; ++i) {
+    p.qs[i] = d->q_strides[i];
+    p.ks[i] = d->k_strides[i];
+    p.vs[i] = d->v_strides[i];
+    p.os[i] = d->o_strides[i];
+  }
+  p.scale = d->scale;
+  const int64_t blocks = d->batch * d->heads * p.num_mtiles;
+  if (blocks > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
+  switch (d->head_dim) {
+    case 16: return launch_d<16>(p, blocks, stream);
+    case 32: return launch_d<32>(p, blocks, stream);
+    case 64: return launch_d<64>(p, blocks, stream);
+    case 128: return launch_d<128>(p, blocks, stream);
+    default: return FPK_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace fpk

@@ -1,0 +1,560 @@
+// f16 fp_attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Computes the reference kernel's result (lib/Plan/TritonEmitter.cpp:73-104,
+// twin python/fusionpass/kernels.py:58-89): O = softmax(scale * Q K^T) V per
+// (batch, head) with an online softmax, never writing the S x S scores.  Q K^T
+// and P V run as f16 x f16 -> f32 UMMAs; the softmax is f32; P is rounded to
+// f16 for the P V product; O is rounded once at the store.
+//
+// CTA = 2 query tiles of 128 rows of one (batch, head), 320 threads:
+//   warps 0-3  softmax warpgroup of tile 0 (one thread per query row)
+//   warps 4-7  softmax warpgroup of tile 1
+//   warp  8    TMA producer: Q once, then K_j / V_j 128-key tiles into a ring
+//   warp  9    TMEM allocator + single-thread UMMA issuer
+// TMEM (512 columns x 128 lanes): S_t at columns 128*t, O_t at 256 + 128*t.
+// P_t (f16, two per column) overwrites the first 64 columns of S_t and feeds
+// the P V UMMA straight from TMEM.  UMMAs issued by one thread execute in
+// order, so Q K^T of the next key tile may be issued into S_t right after the
+// P V UMMA that reads P_t from it.
+//
+// Softmax per row (log2 domain, scale folded into one FFMA per score):
+// m = running max actually used for the exponentials; O and l are rescaled
+// only when the tile max exceeds m by more than 2^8 (P values stay <= 256 and
+// exact in f16 range), which leaves the final O = acc / l unchanged
+// mathematically.  Out-of-range keys of the last tile get p = 0, out-of-range
+// query rows are clipped by the TMA store.
+//
+// Every mbarrier wait is bounded (see common.cuh); on a timeout all roles stop,
+// in-flight TMA loads and UMMAs are drained, TMEM is freed and the kernel
+// returns with FPK_ERR_TIMEOUT in the status word.
+#include <cuda.h>
+
+#include <atomic>
+#include <cmath>
+#include <mutex>
+
+#include "common.cuh"
+#include "internal.h"
+#include "tmem_ops.cuh"
+
+namespace fpk {
+namespace attn_tc {
+
+constexpr int kBM = 128;  // query rows per tile (UMMA M)
+constexpr int kBN = 128;  // keys per iteration
+constexpr int kTiles = 2; // query tiles per CTA
+constexpr int kWG = 128;  // softmax threads per tile
+constexpr int kTmaWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleLog2 = 8.0f;
+constexpr int kMinSmem = 116 * 1024;  // keeps one CTA per SM (it owns all 512 TMEM columns)
+
+template <int D>
+struct Cfg {
+  static constexpr int kBoxCols = D >= 64 ? 64 : D;     // elements per swizzled row
+  static constexpr int kRowBytes = kBoxCols * 2;
+  static constexpr int kBoxes = D / kBoxCols;
+  static constexpr int kBoxBytes = 128 * kRowBytes;     // 128 rows of one box
+  static constexpr int kTileBytes = kBoxes * kBoxBytes; // 128 x D f16
+  static constexpr int kStages = D == 128 ? 2 : 3;
+  static constexpr uint32_t kLayout = D >= 64 ? 2u : (D == 32 ? 4u : 6u);  // SW128 / SW64 / SW32
+  static constexpr uint32_t kSwzMask = D >= 64 ? 7u : (D == 32 ? 3u : 1u);
+  static constexpr int kKStepsPerBox = kRowBytes / 32;  // 16 f16 = 32 B per UMMA k-step
+  static constexpr int kSmemBytes = (kTiles + 2 * kStages) * kTileBytes + 1024;
+  static constexpr int kLaunchSmem = kSmemBytes > kMinSmem ? kSmemBytes : kMinSmem;
+};
+
+struct Params {
+  int* status;
+  int32_t heads;
+  int32_t seq;
+  int32_t num_mblocks;
+  float scale_log2;  // scale * log2(e)
+  uint32_t flags;
+};
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
+  uint64_t s_full[kTiles], p_full[kTiles], o_done[kTiles];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// ------------------------------------------------------------- PTX glue ---
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;  // descriptor version for sm_100
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
+  return d;
+}
+
+// kind::f16 instruction descriptor: f16 A and B, f32 accumulator, A K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool b_mn_major) {
+  return (1u << 4) | (b_mn_major ? (1u << 16) : 0u) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int x, int y, int z,
+                                             int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Bounded wait that ignores the abort flag: used to drain in-flight async work.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* status) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_status(status, FPK_ERR_TIMEOUT);
+      return;
+    }
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t* r) {
+  if constexpr (N == 16) tmem_ld_x16(taddr, r);
+  else if constexpr (N == 32) tmem_ld_x32(taddr, r);
+  else if constexpr (N == 64) tmem_ld_x64(taddr, r);
+  else tmem_ld_x128(taddr, r);
+}
+template <int N>
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t* r) {
+  if constexpr (N == 16) tmem_st_x16(taddr, r);
+  else if constexpr (N == 32) tmem_st_x32(taddr, r);
+  else if constexpr (N == 64) tmem_st_x64(taddr, r);
+  else tmem_st_x128(taddr, r);
+}
+
+// ------------------------------------------------------------- the kernel ---
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                   const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to,
+                   const __grid_constant__ Params p) {
+  using C = Cfg<D>;
+  constexpr int NS = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ Bars bars;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kTiles * C::kTileBytes;
+  uint8_t* sV = sK + NS * C::kTileBytes;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int bh = static_cast<int>(blockIdx.x / p.num_mblocks);
+  const int mb = static_cast<int>(blockIdx.x % p.num_mblocks);
+  const int hh = bh % p.heads;
+  const int bb = bh / p.heads;
+  const int S = p.seq;
+  const int m0 = mb * (kTiles * kBM);
+  const int ntiles = (m0 + kBM < S) ? 2 : 1;
+  const int nkv = (S + kBN - 1) / kBN;
+  const bool test_timeout = (p.flags & FPK_FLAG_TEST_TIMEOUT) != 0;
+  const uint64_t limit = test_timeout ? kTestWaitLimitNs : kWaitLimitNs;
+  volatile int* abort = &bars.abort;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars.q_full, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&bars.k_full[s], 1);
+      mbar_init(&bars.k_empty[s], 1);
+      mbar_init(&bars.v_full[s], 1);
+      mbar_init(&bars.v_empty[s], 1);
+    }
+    for (int t = 0; t < kTiles; ++t) {
+      mbar_init(&bars.s_full[t], 1);
+      mbar_init(&bars.p_full[t], kWG);
+      mbar_init(&bars.o_done[t], 1);
+    }
+    mbar_init(&bars.drain, 1);
+    bars.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&bars.tmem_base)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars.tmem_base;
+
+  if (warp == kTmaWarp) {
+    // --------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      bool q_issued = false;
+      int last_k[NS], last_v[NS];
+      for (int s = 0; s < NS; ++s) last_k[s] = last_v[s] = -1;
+      if (!test_timeout) {  // the timeout test withholds Q on purpose
+        mbar_arrive_expect_tx(&bars.q_full, static_cast<uint32_t>(ntiles * C::kTileBytes));
+        for (int t = 0; t < ntiles; ++t)
+          for (int bx = 0; bx < C::kBoxes; ++bx)
+            tma_load_4d(sQ + t * C::kTileBytes + bx * C::kBoxBytes, &tq, bx * C::kBoxCols, m0 + t * kBM, hh,
+                        bb, &bars.q_full);
+        q_issued = true;
+      }
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j % NS;
+        const uint32_t r = static_cast<uint32_t>(j / NS);
+        if (!mbar_wait(&bars.k_empty[s], (r & 1u) ^ 1u, abort, p.status, limit)) break;
+        mbar_arrive_expect_tx(&bars.k_full[s], C::kTileBytes);
+        for (int bx = 0; bx < C::kBoxes; ++bx)
+          tma_load_4d(sK + s * C::kTileBytes + bx * C::kBoxBytes, &tk, bx * C::kBoxCols, j * kBN, hh, bb,
+                      &bars.k_full[s]);
+        last_k[s] = j;
+        if (!mbar_wait(&bars.v_empty[s], (r & 1u) ^ 1u, abort, p.status, limit)) break;
+        mbar_arrive_expect_tx(&bars.v_full[s], C::kTileBytes);
+        for (int bx = 0; bx < C::kBoxes; ++bx)
+          tma_load_4d(sV + s * C::kTileBytes + bx * C::kBoxBytes, &tv, bx * C::kBoxCols, j * kBN, hh, bb,
+                      &bars.v_full[s]);
+        last_v[s] = j;
+      }
+      // no TMA write may land after the CTA has gone
+      if (q_issued) drain_wait(&bars.q_full, 0, p.status);
+      for (int s = 0; s < NS; ++s) {
+        if (last_k[s] >= 0) drain_wait(&bars.k_full[s], static_cast<uint32_t>(last_k[s] / NS) & 1u, p.status);
+        if (last_v[s] >= 0) drain_wait(&bars.v_full[s], static_cast<uint32_t>(last_v[s] / NS) & 1u, p.status);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ----------------------------------------------------------- UMMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_f16(kBM, kBN, false);
+      constexpr uint32_t idesc_pv = idesc_f16(kBM, D, true);
+      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      auto issue_qk = [&](int t, int s) {
+        const uint32_t d_tmem = tbase + static_cast<uint32_t>(t * 128);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk / C::kKStepsPerBox) * C::kBoxBytes + (kk % C::kKStepsPerBox) * 32;
+          const uint64_t a = sdesc(q_addr + t * C::kTileBytes + off, 16, 8 * C::kRowBytes, C::kLayout);
+          const uint64_t b = sdesc(k_addr + s * C::kTileBytes + off, 16, 8 * C::kRowBytes, C::kLayout);
+          mma_ss(d_tmem, a, b, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int t, int s, bool accumulate) {
+        const uint32_t d_tmem = tbase + 256u + static_cast<uint32_t>(t * 128);
+        const uint32_t a_tmem = tbase + static_cast<uint32_t>(t * 128);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t b = sdesc(v_addr + s * C::kTileBytes + kk * 16 * C::kRowBytes, C::kBoxBytes,
+                                   8 * C::kRowBytes, C::kLayout);
+          mma_ts(d_tmem, a_tmem + static_cast<uint32_t>(kk * 8), b, idesc_pv, (accumulate || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(&bars.q_full, 0, abort, p.status, limit) &&
+                mbar_wait(&bars.k_full[0], 0, abort, p.status, limit);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < ntiles; ++t) {
+          issue_qk(t, 0);
+          mma_commit(&bars.s_full[t]);
+        }
+        mma_commit(&bars.k_empty[0]);
+      }
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int s = j % NS;
+        const uint32_t r = static_cast<uint32_t>(j / NS);
+        const bool more = j + 1 < nkv;
+        const int s1 = (j + 1) % NS;
+        const uint32_t r1 = static_cast<uint32_t>((j + 1) / NS);
+        if (!mbar_wait(&bars.v_full[s], r & 1u, abort, p.status, limit)) break;
+        for (int t = 0; t < ntiles; ++t) {
+          if (!mbar_wait(&bars.p_full[t], static_cast<uint32_t>(j) & 1u, abort, p.status, limit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(t, s, j > 0);
+          mma_commit(&bars.o_done[t]);
+          if (more) {
+            if (t == 0 && !mbar_wait(&bars.k_full[s1], r1 & 1u, abort, p.status, limit)) {
+              ok = false;
+              break;
+            }
+            issue_qk(t, s1);
+            mma_commit(&bars.s_full[t]);
+          }
+        }
+        if (!ok) break;
+        mma_commit(&bars.v_empty[s]);
+        if (more) mma_commit(&bars.k_empty[s1]);
+      }
+      // every UMMA issued so far must finish before TMEM is freed
+      mma_commit(&bars.drain);
+      drain_wait(&bars.drain, 0, p.status);
+    }
+  } else {
+    // ------------------------------------------------------ softmax + epilogue
+    const int t = warp >> 2;
+    const int row = threadIdx.x & (kWG - 1);
+    if (t < ntiles) {
+      const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+      const uint32_t tS = tbase + lane_off + static_cast<uint32_t>(t * 128);
+      const uint32_t tO = tbase + lane_off + 256u + static_cast<uint32_t>(t * 128);
+      const float k2 = p.scale_log2;
+      float m_run = -INFINITY;
+      float l = 0.0f;
+      bool ok = true;
+      for (int j = 0; j < nkv; ++j) {
+        if (!mbar_wait(&bars.s_full[t], static_cast<uint32_t>(j) & 1u, abort, p.status, limit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sr[128];
+        tmem_ld_x128(tS, sr);
+        const int valid = S - j * kBN;  // > 0; < 128 only on the last tile
+        float mx = -INFINITY;
+        if (valid >= kBN) {
+          if (k2 >= 0.0f) {
+#pragma unroll
+            for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+          } else {
+            mx = INFINITY;
+#pragma unroll
+            for (int c = 0; c < kBN; ++c) mx = fminf(mx, __uint_as_float(sr[c]));
+          }
+        } else {
+          if (k2 >= 0.0f) {
+#pragma unroll
+            for (int c = 0; c < kBN; ++c)
+              if (c < valid) mx = fmaxf(mx, __uint_as_float(sr[c]));
+          } else {
+            mx = INFINITY;
+#pragma unroll
+            for (int c = 0; c < kBN; ++c)
+              if (c < valid) mx = fminf(mx, __uint_as_float(sr[c]));
+          }
+        }
+        mx *= k2;  // row max of the log2-scaled scores
+        if (j == 0) {
+          m_run = mx;
+        } else {
+          const bool need = mx > m_run + kRescaleLog2;
+          if (__any_sync(0xffffffffu, need)) {
+            const float alpha = need ? ex2(m_run - mx) : 1.0f;
+            if (need) m_run = mx;
+            l *= alpha;
+            // O_t already holds P_{j-1} V_{j-1}: the commit that signalled S_t
+            // covers every earlier UMMA of this CTA.
+            constexpr int kChunk = D < 32 ? D : 32;
+#pragma unroll
+            for (int c0 = 0; c0 < D; c0 += kChunk) {
+              uint32_t orow[kChunk];
+              tmem_ld<kChunk>(tO + static_cast<uint32_t>(c0), orow);
+#pragma unroll
+              for (int c = 0; c < kChunk; ++c) orow[c] = __float_as_uint(__uint_as_float(orow[c]) * alpha);
+              tmem_st<kChunk>(tO + static_cast<uint32_t>(c0), orow);
+            }
+          }
+        }
+        const float neg_m = -m_run;
+        float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        uint32_t pk[64];
+#pragma unroll
+        for (int c = 0; c < kBN; c += 2) {
+          float p0 = ex2(fmaf(__uint_as_float(sr[c]), k2, neg_m));
+          float p1 = ex2(fmaf(__uint_as_float(sr[c + 1]), k2, neg_m));
+          if (valid < kBN) {
+            p0 = c < valid ? p0 : 0.0f;
+            p1 = c + 1 < valid ? p1 : 0.0f;
+          }
+          ls[(c >> 1) & 3] += p0 + p1;
+          pk[c >> 1] = pack_half2(p0, p1);
+        }
+        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        tmem_st_x64(tS, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bars.p_full[t]);
+      }
+      // epilogue: O / l -> f16 -> swizzled staging (the Q_t buffer) -> TMA store
+      if (ok && mbar_wait(&bars.o_done[t], static_cast<uint32_t>(nkv - 1) & 1u, abort, p.status, limit)) {
+        tc_fence_after();
+        uint8_t* stage = sQ + t * C::kTileBytes;
+        constexpr int kChunk = D < 32 ? D : 32;
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += kChunk) {
+          uint32_t orow[kChunk];
+          tmem_ld<kChunk>(tO + static_cast<uint32_t>(c0), orow);
+          uint32_t h2[kChunk / 2];
+#pragma unroll
+          for (int c = 0; c < kChunk; c += 2)
+            h2[c / 2] = pack_half2(__fdiv_rn(__uint_as_float(orow[c]), l),
+                                   __fdiv_rn(__uint_as_float(orow[c + 1]), l));
+#pragma unroll
+          for (int q = 0; q < kChunk / 8; ++q) {
+            const int col = c0 + q * 8;  // first element of this 16-byte chunk
+            const int bx = col / C::kBoxCols;
+            const uint32_t off = static_cast<uint32_t>(row * C::kRowBytes + (col % C::kBoxCols) * 2);
+            const uint32_t phys = off ^ (((off >> 7) & C::kSwzMask) << 4);
+            *reinterpret_cast<uint4*>(stage + bx * C::kBoxBytes + phys) =
+                make_uint4(h2[q * 4], h2[q * 4 + 1], h2[q * 4 + 2], h2[q * 4 + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(1 + t, kWG);
+        if (row == 0) {
+          for (int bx = 0; bx < C::kBoxes; ++bx)
+            tma_store_4d(&to, stage + bx * C::kBoxBytes, bx * C::kBoxCols, m0 + t * kBM, hh, bb);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kTmemCols));
+  }
+}
+
+// ------------------------------------------------------------- host side ---
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encoder() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 4-D map over [batch, heads, seq, D] (dims listed innermost first), 128-row boxes.
+static int make_map(CUtensorMap* m, const void* base, const int64_t* st, const fpk_attn_desc* d) {
+  EncodeTiledFn enc = encoder();
+  if (!enc) return FPK_ERR_CUDA;
+  const int D = d->head_dim;
+  if (reinterpret_cast<uintptr_t>(base) % 16) return FPK_ERR_ALIGN;
+  for (int i = 0; i < 3; ++i)
+    if (st[i] <= 0 || (st[i] * 2) % 16) return FPK_ERR_ALIGN;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(d->seq_len),
+                              static_cast<cuuint64_t>(d->heads), static_cast<cuuint64_t>(d->batch)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(st[2] * 2), static_cast<cuuint64_t>(st[1] * 2),
+                                 static_cast<cuuint64_t>(st[0] * 2)};
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(D >= 64 ? 64 : D), 128u, 1u, 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  const CUtensorMapSwizzle swz = D >= 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                         : (D == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FPK_OK : FPK_ERR_INVALID;
+}
+
+template <int D>
+static int launch_d(const CUtensorMap* maps, const Params& p, int64_t blocks, cudaStream_t s) {
+  static std::atomic<int> opted[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FPK_ERR_CUDA;
+  if (!opted[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(attn_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg<D>::kLaunchSmem) != cudaSuccess)
+      return FPK_ERR_CUDA;
+    opted[dev].store(1, std::memory_order_release);
+  }
+  attn_tc_kernel<D><<<static_cast<unsigned>(blocks), kThreads, Cfg<D>::kLaunchSmem, s>>>(maps[0], maps[1], maps[2],
+                                                                                        maps[3], p);
+  return cudaGetLastError() == cudaSuccess ? FPK_OK : FPK_ERR_CUDA;
+}
+
+}  // namespace attn_tc
+
+int launch_attention_tc(const fpk_attn_desc* d, const void* q, const void* k, const void* v, void* o,
+                        cudaStream_t stream, const DeviceInfo& dev) {
+  using namespace attn_tc;
+  if (d->seq_len > 0x7fffffffLL || d->heads > 0x7fffffffLL || d->batch > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
+  CUtensorMap maps[4];
+  int rc;
+  if ((rc = make_map(&maps[0], q, d->q_strides, d)) != FPK_OK) return rc;
+  if ((rc = make_map(&maps[1], k, d->k_strides, d)) != FPK_OK) return rc;
+  if ((rc = make_map(&maps[2], v, d->v_strides, d)) != FPK_OK) return rc;
+  if ((rc = make_map(&maps[3], o, d->o_strides, d)) != FPK_OK) return rc;
+  Params p;
+  p.status = dev.status;
+  p.heads = static_cast<int32_t>(d->heads);
+  p.seq = static_cast<int32_t>(d->seq_len);
+  p.num_mblocks = static_cast<int32_t>((d->seq_len + kTiles * kBM - 1) / (kTiles * kBM));
+  p.scale_log2 = d->scale * 1.4426950408889634f;
+  p.flags = d->flags;
+  const int64_t blocks = d->batch * d->heads * p.num_mblocks;
+  if (blocks > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
+  switch (d->head_dim) {
+    case 16: return launch_d<16>(maps, p, blocks, stream);
+    case 32: return launch_d<32>(maps, p, blocks, stream);
+    case 64: return launch_d<64>(maps, p, blocks, stream);
+    case 128: return launch_d<128>(maps, p, blocks, stream);
+    default: return FPK_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace fpk

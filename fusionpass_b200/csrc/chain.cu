@@ -1,0 +1,902 @@
+// Fused elementwise chains: the sm_100a replacement of the reference's
+// generated fp_chain_<N> Triton kernels (lib/Plan/TritonEmitter.cpp:14-65,
+// twin python/fusionpass/kernels.py:129-211).
+//
+// One prebuilt kernel per launch mode interprets the compiled op list, so no
+// code is generated per model.  The host compiles the descriptor's op DAG into
+// an accumulator micro-program: one running value `acc`, the loaded inputs and
+// four spill registers, each holding V consecutive elements of the thread.  A
+// micro-op is one warp-uniform branch followed by V f32 operations, so the
+// dispatch cost is amortised over V elements and every value stays in
+// registers.  Arithmetic is f32 with explicit round-to-nearest adds and
+// multiplies (no FMA contraction), and the result is rounded once at the
+// store, as the reference kernels do.
+//
+// flat: a persistent grid (1 CTA per SM).  One producer warp streams whole
+//   7680-element tiles of every full-shape operand into a ring of shared
+//   memory stages with 1-D TMA bulk copies (cp.async.bulk + mbarrier
+//   complete_tx, L2 evict_first); 15 consumer warps evaluate the program from
+//   shared memory and write 8- or 16-byte vectors straight to HBM.
+//   Broadcast operands (per-column vector, per-row value, scalar) are read
+//   through the read-only cache with incrementally tracked row/column indices.
+// rows: one warp (cols <= 1024) or one CTA (cols <= 16384) per row; the
+//   softmax input of the whole row stays in registers, max and sum are reduced
+//   with warp shuffles (+ shared memory across warps), then the post-softmax
+//   ops run and the row is stored.
+#include <atomic>
+#include <cmath>
+#include <cstring>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace fpk {
+namespace chain {
+
+constexpr int kMaxIn = FPK_CHAIN_MAX_INPUTS;
+constexpr int kNumTmp = 4;
+constexpr int kMaxCode = 112;
+
+// ----------------------------------------------------------- micro-ops ---
+enum : int {
+  C_MOV_IN = 0,   // 0..7   acc = in[i]
+  C_MOV_T = 8,    // 8..11  acc = t[j]
+  C_SAVE_T = 12,  // 12..15 t[j] = acc
+  C_ADD_IN = 16,  // 16..23 acc = acc + in[i]
+  C_ADD_T = 24,   // 24..27 acc = acc + t[j]
+  C_ADD_ACC = 28, //        acc = acc + acc
+  C_MUL_IN = 32,  // 32..39 acc = acc * in[i]
+  C_MUL_T = 40,   // 40..43 acc = acc * t[j]
+  C_MUL_ACC = 44, //        acc = acc * acc
+  C_SCALE = 48,   //        acc = acc * imm
+  C_RELU = 49,
+  C_EXP = 50,
+  C_GELU = 51,
+  C_SOFTMAX = 52, // rows mode split point
+};
+
+// how the kernel reads an input
+enum : int {
+  M_STAGED = 0,      // full shape, TMA-staged through shared memory (flat only)
+  M_FULL_VEC = 1,    // full shape, aligned vector loads
+  M_FULL_SCALAR = 2, // full shape, element loads
+  M_COL_VEC = 3,     // per-column vector, cols % 4 == 0, aligned
+  M_COL_SCALAR = 4,  // per-column vector, element loads
+  M_ROW = 5,         // one value per row
+  M_SCALAR = 6,      // single value
+  M_NONE = 7,        // unused input slot of a wider template instance
+};
+
+struct Input {
+  const void* ptr;
+  int32_t dtype;
+  int32_t mode;
+  uint32_t smem_off;
+  int32_t pad;
+};
+
+struct Params {
+  Input in[kMaxIn];
+  void* out;
+  int* status;
+  int64_t numel, rows, cols;
+  int64_t num_tiles;
+  int64_t row_step_t;   // flat: whole rows advanced per tile step (grid * tile)
+  uint32_t col_step_t;  // flat: column advance per tile step, mod cols
+  uint32_t col_step_q;  // flat: column advance per quad step inside a tile, mod cols
+  uint32_t row_step_q;  // flat: whole rows advanced per quad step inside a tile
+  int32_t out_dtype;
+  int32_t out_vec;
+  int32_t n_code;
+  int32_t n_pre;        // rows: index of the SOFTMAX micro-op
+  int32_t post_reload;  // rows: post-softmax ops read inputs or spill registers
+  int32_t stage_bytes;
+  int32_t nstage;
+  int32_t need_idx;     // flat: some operand needs the row/column index
+  uint32_t flags;
+  uint8_t code[kMaxCode];
+  float imm[kMaxCode];
+};
+
+// ------------------------------------------------------- f32 element ops ---
+__device__ __forceinline__ float op_relu(float x) { return x != x ? x : fmaxf(x, 0.0f); }
+
+__device__ __forceinline__ float op_gelu(float x) {
+  const float t = __fmul_rn(x, 0.70710678118654752f);
+  const float e = erff(t);
+  return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.0f, e));
+}
+
+template <int NIN, int V, int NT = kNumTmp>
+struct Regs {
+  float in[NIN][V];
+  float t[NT > 0 ? NT : 1][V];
+  float acc[V];
+};
+
+// Run micro-ops [pc0, pc1) of the program over the V elements held in R.
+template <int NIN, int V, int NT>
+__device__ __forceinline__ void run_code(const Params& p, int pc0, int pc1, Regs<NIN, V, NT>& R) {
+#pragma unroll 1
+  for (int pc = pc0; pc < pc1; ++pc) {
+    const int c = p.code[pc];
+    switch (c) {
+#define FPK_IN_CASES(I)                                                          \
+  case C_MOV_IN + I:                                                             \
+    if constexpr (I < NIN) {                                                     \
+      _Pragma("unroll") for (int e = 0; e < V; ++e) R.acc[e] = R.in[I][e];       \
+    }                                                                            \
+    break;                                                                       \
+  case C_ADD_IN + I:                                                             \
+    if constexpr (I < NIN) {                                                     \
+      _Pragma("unroll") for (int e = 0; e < V; ++e) R.acc[e] =                   \
+          __fadd_rn(R.acc[e], R.in[I][e]);                                       \
+    }                                                                            \
+    break;                                                                       \
+  case C_MUL_IN + I:                                                             \
+    if constexpr (I < NIN) {                                                     \
+      _Pragma("unroll") for (int e = 0; e < V; ++e) R.acc[e] =                   \
+          __fmul_rn(R.acc[e], R.in[I][e]);                                       \
+    }                                                                            \
+    break;
+      FPK_IN_CASES(0)
+      FPK_IN_CASES(1)
+      FPK_IN_CASES(2)
+      FPK_IN_CASES(3)
+      FPK_IN_CASES(4)
+      FPK_IN_CASES(5)
+      FPK_IN_CASES(6)
+      FPK_IN_CASES(7)
+#undef FPK_IN_CASES
+#define FPK_T_CASES(J)                                                                        \
+  case C_MOV_T + J:                                                                           \
+    if constexpr (J < NT) {                                                                   \
+      _Pragma("unroll") for (int e = 0; e < V; ++e) R.acc[e] = R.t[J][e];                     \
+    }                                                                                         \
+    break;                                                                                    \
+  case C_SAVE_T + J:                                                                          \
+    if constexpr (J < NT) {                                                                   \
+      _Pragma("unroll") for (int e = 0; e < V; ++e) R.t[J][e] = R.acc[e];                     \
+    }                                                                                         \
+    break;                                                                                    \
+  case C_ADD_T + J:                                                                           \
+    if constexpr (J < NT) {                                                                   \
+      _Pragma("unroll") for (int e = 0; e < V; ++e) R.acc[e] = __fadd_rn(R.acc[e], R.t[J][e]); \
+    }                                                                                         \
+    break;                                                                                    \
+  case C_MUL_T + J:                                                                           \
+    if constexpr (J < NT) {                                                                   \
+      _Pragma("unroll") for (int e = 0; e < V; ++e) R.acc[e] = __fmul_rn(R.acc[e], R.t[J][e]); \
+    }                                                                                         \
+    break;
+      FPK_T_CASES(0)
+      FPK_T_CASES(1)
+      FPK_T_CASES(2)
+      FPK_T_CASES(3)
+#undef FPK_T_CASES
+      case C_ADD_ACC:
+#pragma unroll
+        for (int e = 0; e < V; ++e) R.acc[e] = __fadd_rn(R.acc[e], R.acc[e]);
+        break;
+      case C_MUL_ACC:
+#pragma unroll
+        for (int e = 0; e < V; ++e) R.acc[e] = __fmul_rn(R.acc[e], R.acc[e]);
+        break;
+      case C_SCALE: {
+        const float s = p.imm[pc];
+#pragma unroll
+        for (int e = 0; e < V; ++e) R.acc[e] = __fmul_rn(R.acc[e], s);
+        break;
+      }
+      case C_RELU:
+#pragma unroll
+        for (int e = 0; e < V; ++e) R.acc[e] = op_relu(R.acc[e]);
+        break;
+      case C_EXP:
+#pragma unroll
+        for (int e = 0; e < V; ++e) R.acc[e] = expf(R.acc[e]);
+        break;
+      case C_GELU:
+#pragma unroll
+        for (int e = 0; e < V; ++e) R.acc[e] = op_gelu(R.acc[e]);
+        break;
+      default:
+        break;
+    }
+  }
+}
+
+// --------------------------------------------------------------- loads ---
+// All loaders return a float4 by value so the caller's register arrays are only
+// ever indexed with compile-time constants (no local-memory copies).
+__device__ __forceinline__ float ld1(const void* base, int64_t idx, int dtype) {
+  if (dtype == FPK_F16) return __half2float(__ldg(reinterpret_cast<const __half*>(base) + idx));
+  return __ldg(reinterpret_cast<const float*>(base) + idx);
+}
+
+__device__ __forceinline__ float4 splat(float x) { return make_float4(x, x, x, x); }
+
+__device__ __forceinline__ float4 h4_to_f4(uint2 u) {
+  const float2 a = unpack_half2(u.x), b = unpack_half2(u.y);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// 4 consecutive elements at element index idx (aligned: 8 B for f16, 16 B for f32)
+__device__ __forceinline__ float4 ld4_vec(const void* base, int64_t idx, int dtype) {
+  if (dtype == FPK_F16)
+    return h4_to_f4(__ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(base) + idx)));
+  return __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx));
+}
+
+// streaming (read-once) variant for full-shape operands that are not staged
+__device__ __forceinline__ float4 ld4_stream(const void* base, int64_t idx, int dtype) {
+  if (dtype == FPK_F16)
+    return h4_to_f4(__ldcs(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(base) + idx)));
+  return __ldcs(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx));
+}
+
+__device__ __forceinline__ float4 lds4(const uint8_t* p, int dtype) {
+  if (dtype == FPK_F16) return h4_to_f4(*reinterpret_cast<const uint2*>(p));
+  return *reinterpret_cast<const float4*>(p);
+}
+
+// Element-wise loads of the quad starting at flat index e (e + j >= numel reads 0).
+__device__ __forceinline__ float4 load_quad_slow(const Input& in, int64_t e, int64_t numel, int64_t cols) {
+  float r[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t x = e + j;
+    float v = 0.0f;
+    if (x < numel) {
+      switch (in.mode) {
+        case M_COL_VEC:
+        case M_COL_SCALAR: v = ld1(in.ptr, x % cols, in.dtype); break;
+        case M_ROW: v = ld1(in.ptr, x / cols, in.dtype); break;
+        case M_SCALAR: v = ld1(in.ptr, 0, in.dtype); break;
+        default: v = ld1(in.ptr, x, in.dtype); break;  // full shape (staged or not)
+      }
+    }
+    r[j] = v;
+  }
+  return make_float4(r[0], r[1], r[2], r[3]);
+}
+
+// Quad of input `in` for row `row`, columns [c, c + nv) of a rows-mode chain.
+__device__ __forceinline__ float4 load_quad_row(const Input& in, int64_t row, int64_t rbase, int64_t c, int nv) {
+  switch (in.mode) {
+    case M_FULL_VEC: return ld4_vec(in.ptr, rbase + c, in.dtype);
+    case M_COL_VEC: return ld4_vec(in.ptr, c, in.dtype);
+    case M_ROW: return splat(ld1(in.ptr, row, in.dtype));
+    case M_SCALAR: return splat(ld1(in.ptr, 0, in.dtype));
+    case M_COL_SCALAR: {
+      float r[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] = j < nv ? ld1(in.ptr, c + j, in.dtype) : 0.0f;
+      return make_float4(r[0], r[1], r[2], r[3]);
+    }
+    default: {  // full shape, element loads
+      float r[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] = j < nv ? ld1(in.ptr, rbase + c + j, in.dtype) : 0.0f;
+      return make_float4(r[0], r[1], r[2], r[3]);
+    }
+  }
+}
+
+template <int NIN, int V, int NT>
+__device__ __forceinline__ void put4(Regs<NIN, V, NT>& R, int i, int at, float4 v) {
+  R.in[i][at + 0] = v.x;
+  R.in[i][at + 1] = v.y;
+  R.in[i][at + 2] = v.z;
+  R.in[i][at + 3] = v.w;
+}
+
+// Store 4 consecutive outputs at element index idx; `n` (1..4) valid ones.
+__device__ __forceinline__ void st4(const Params& p, int64_t idx, float4 v, int n) {
+  if (p.out_dtype == FPK_F16) {
+    __half* o = reinterpret_cast<__half*>(p.out) + idx;
+    if (n == 4 && p.out_vec) {
+      uint2 u;
+      u.x = pack_half2(v.x, v.y);
+      u.y = pack_half2(v.z, v.w);
+      *reinterpret_cast<uint2*>(o) = u;
+    } else {
+      if (n > 0) o[0] = __float2half_rn(v.x);
+      if (n > 1) o[1] = __float2half_rn(v.y);
+      if (n > 2) o[2] = __float2half_rn(v.z);
+      if (n > 3) o[3] = __float2half_rn(v.w);
+    }
+  } else {
+    float* o = reinterpret_cast<float*>(p.out) + idx;
+    if (n == 4 && p.out_vec) {
+      *reinterpret_cast<float4*>(o) = v;
+    } else {
+      if (n > 0) o[0] = v.x;
+      if (n > 1) o[1] = v.y;
+      if (n > 2) o[2] = v.z;
+      if (n > 3) o[3] = v.w;
+    }
+  }
+}
+
+template <int NIN, int V, int NT>
+__device__ __forceinline__ float4 acc4(const Regs<NIN, V, NT>& R, int at) {
+  return make_float4(R.acc[at], R.acc[at + 1], R.acc[at + 2], R.acc[at + 3]);
+}
+
+// ================================================================ flat ===
+constexpr int kConsumerWarps = 15;
+constexpr int kNCT = kConsumerWarps * 32;  // consumer threads
+constexpr int kQPT = 4;                    // quads per consumer thread per tile
+constexpr int kTile = kNCT * kQPT * 4;     // 7680 elements
+constexpr int kFlatThreads = kNCT + 32;    // + 1 producer warp
+constexpr int kMaxStages = 8;
+constexpr int kMaxStageBytes = 64 * 1024;
+constexpr int kStageBudget = 192 * 1024;
+
+template <int NIN, int NT>
+__global__ void __launch_bounds__(kFlatThreads, 1) chain_flat_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full_bar[kMaxStages];
+  __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nstage = p.nstage;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nstage; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kConsumerWarps);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const uint64_t limit = (p.flags & FPK_FLAG_TEST_TIMEOUT) ? kTestWaitLimitNs : kWaitLimitNs;
+  const int64_t G = gridDim.x;
+
+  if (warp == kConsumerWarps) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      int64_t last_li[kMaxStages];
+      for (int s = 0; s < kMaxStages; ++s) last_li[s] = -1;
+      int64_t li = 0;
+      for (int64_t tile = blockIdx.x; tile < p.num_tiles; tile += G, ++li) {
+        const int s = static_cast<int>(li % nstage);
+        const uint32_t r = static_cast<uint32_t>(li / nstage);
+        if (!mbar_wait(&empty_bar[s], (r & 1u) ^ 1u, &abort_flag, p.status, limit)) break;
+        if ((p.flags & FPK_FLAG_TEST_TIMEOUT) && li == 0) continue;  // withheld on purpose
+        const int64_t e0 = tile * kTile;
+        const bool whole = e0 + kTile <= p.numel;
+        if (whole && p.stage_bytes > 0) {
+          mbar_arrive_expect_tx(&full_bar[s], static_cast<uint32_t>(p.stage_bytes));
+          uint8_t* dst = smem + static_cast<size_t>(s) * p.stage_bytes;
+#pragma unroll
+          for (int i = 0; i < NIN; ++i) {
+            if (p.in[i].mode == M_STAGED) {
+              const int esz = p.in[i].dtype == FPK_F16 ? 2 : 4;
+              bulk_g2s(dst + p.in[i].smem_off,
+                       reinterpret_cast<const uint8_t*>(p.in[i].ptr) + e0 * esz,
+                       static_cast<uint32_t>(kTile * esz), &full_bar[s], pol);
+            }
+          }
+          last_li[s] = li;
+        } else {
+          mbar_arrive(&full_bar[s]);
+        }
+      }
+      // Drain: no bulk copy may still be in flight when the CTA exits.
+      for (int s = 0; s < nstage; ++s) {
+        if (last_li[s] < 0) continue;
+        const uint32_t par = static_cast<uint32_t>(last_li[s] / nstage) & 1u;
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full_bar[s], par)) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            record_status(p.status, FPK_ERR_TIMEOUT);
+            break;
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  const int ct = threadIdx.x;
+  const int64_t cols = p.cols;
+  // column / row of this thread's first quad of its first tile
+  int64_t col_b = 0, row_b = 0;
+  if (p.need_idx) {
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * kTile + 4 * ct;
+    col_b = e % cols;
+    row_b = e / cols;
+  }
+  int64_t li = 0;
+  for (int64_t tile = blockIdx.x; tile < p.num_tiles; tile += G, ++li) {
+    const int s = static_cast<int>(li % nstage);
+    const uint32_t r = static_cast<uint32_t>(li / nstage);
+    if (!mbar_wait(&full_bar[s], r & 1u, &abort_flag, p.status, limit)) break;
+    const int64_t e0 = tile * kTile;
+    const bool whole = e0 + kTile <= p.numel;
+    const uint8_t* stage = smem + static_cast<size_t>(s) * p.stage_bytes;
+    int64_t col = col_b, row = row_b;
+
+#pragma unroll 1
+    for (int qp = 0; qp < kQPT; qp += 2) {
+      Regs<NIN, 8, NT> R;
+      int64_t qcol[2], qrow[2];
+      qcol[0] = col; qrow[0] = row;
+      col += p.col_step_q; row += p.row_step_q;
+      if (col >= cols) { col -= cols; ++row; }
+      qcol[1] = col; qrow[1] = row;
+      col += p.col_step_q; row += p.row_step_q;
+      if (col >= cols) { col -= cols; ++row; }
+
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int o = 4 * (ct + kNCT * (qp + h));  // element offset inside the tile
+        const int64_t e = e0 + o;
+#pragma unroll
+        for (int i = 0; i < NIN; ++i) {
+          const Input& in = p.in[i];
+          if (in.mode == M_NONE) continue;
+          float4 v;
+          if (!whole) {
+            v = load_quad_slow(in, e, p.numel, cols);
+          } else {
+            switch (in.mode) {
+              case M_STAGED: v = lds4(stage + in.smem_off + o * (in.dtype == FPK_F16 ? 2 : 4), in.dtype); break;
+              case M_FULL_VEC: v = ld4_stream(in.ptr, e, in.dtype); break;
+              case M_COL_VEC: v = ld4_vec(in.ptr, qcol[h], in.dtype); break;
+              case M_ROW:
+                v = p.need_idx ? splat(ld1(in.ptr, qrow[h], in.dtype)) : load_quad_slow(in, e, p.numel, cols);
+                break;
+              case M_SCALAR: v = splat(ld1(in.ptr, 0, in.dtype)); break;
+              default: v = load_quad_slow(in, e, p.numel, cols); break;
+            }
+          }
+          put4(R, i, 4 * h, v);
+        }
+      }
+      run_code(p, 0, p.n_code, R);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int64_t e = e0 + 4 * (ct + kNCT * (qp + h));
+        if (whole) {
+          st4(p, e, acc4(R, 4 * h), 4);
+        } else if (e < p.numel) {
+          const int64_t rem = p.numel - e;
+          st4(p, e, acc4(R, 4 * h), rem < 4 ? static_cast<int>(rem) : 4);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[s]);
+    if (p.need_idx) {
+      col_b += p.col_step_t;
+      row_b += p.row_step_t;
+      if (col_b >= cols) { col_b -= cols; ++row_b; }
+    }
+  }
+}
+
+// ================================================================ rows ===
+template <int NIN, int TPR, int QPT>
+__global__ void __launch_bounds__(TPR > 32 ? TPR : 256) chain_rows_kernel(const __grid_constant__ Params p) {
+  constexpr int kWarpsPerRow = TPR / 32;
+  __shared__ float red[2][kWarpsPerRow > 1 ? kWarpsPerRow : 1];
+  const int lane = threadIdx.x & 31;
+  const int64_t cols = p.cols;
+
+  int64_t row, row_step;
+  int lt;  // thread index inside its row group
+  if constexpr (TPR == 32) {
+    const int wpb = blockDim.x >> 5;
+    row = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5);
+    row_step = static_cast<int64_t>(gridDim.x) * wpb;
+    lt = lane;
+  } else {
+    row = blockIdx.x;
+    row_step = gridDim.x;
+    lt = threadIdx.x;
+  }
+  const int pre_end = p.n_pre;
+  const int post_begin = p.n_pre + 1;
+
+  for (; row < p.rows; row += row_step) {
+    float sv[QPT][4];
+    float m = -INFINITY;
+    const int64_t rbase = row * cols;
+#pragma unroll
+    for (int q = 0; q < QPT; ++q) {
+      const int64_t c = 4 * (lt + static_cast<int64_t>(TPR) * q);
+      Regs<NIN, 4> R;
+      if (c < cols) {
+        const int nv = cols - c < 4 ? static_cast<int>(cols - c) : 4;
+#pragma unroll
+        for (int i = 0; i < NIN; ++i) {
+          const Input& in = p.in[i];
+          if (in.mode == M_NONE) continue;
+          put4(R, i, 0, load_quad_row(in, row, rbase, c, nv));
+        }
+        run_code(p, 0, pre_end, R);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sv[q][j] = j < nv ? R.acc[j] : -INFINITY;
+          m = fmaxf(m, sv[q][j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sv[q][j] = -INFINITY;
+      }
+    }
+    // row max
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if constexpr (kWarpsPerRow > 1) {
+      if (lane == 0) red[0][threadIdx.x >> 5] = m;
+      __syncthreads();
+      m = red[0][0];
+#pragma unroll
+      for (int w = 1; w < kWarpsPerRow; ++w) m = fmaxf(m, red[0][w]);
+    }
+    // exp and row sum
+    float sum = 0.0f;
+#pragma unroll
+    for (int q = 0; q < QPT; ++q) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float x = sv[q][j];
+        const float ev = (x == -INFINITY) ? 0.0f : expf(__fsub_rn(x, m));
+        sv[q][j] = ev;
+        sum = __fadd_rn(sum, ev);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
+    if constexpr (kWarpsPerRow > 1) {
+      if (lane == 0) red[1][threadIdx.x >> 5] = sum;
+      __syncthreads();
+      sum = red[1][0];
+#pragma unroll
+      for (int w = 1; w < kWarpsPerRow; ++w) sum = __fadd_rn(sum, red[1][w]);
+      __syncthreads();  // red[] is reused by the next row
+    }
+    // post-softmax ops and store
+#pragma unroll
+    for (int q = 0; q < QPT; ++q) {
+      const int64_t c = 4 * (lt + static_cast<int64_t>(TPR) * q);
+      if (c >= cols) continue;
+      const int nv = cols - c < 4 ? static_cast<int>(cols - c) : 4;
+      Regs<NIN, 4> R;
+      if (p.post_reload) {
+#pragma unroll
+        for (int i = 0; i < NIN; ++i) {
+          const Input& in = p.in[i];
+          if (in.mode == M_NONE) continue;
+          put4(R, i, 0, load_quad_row(in, row, rbase, c, nv));
+        }
+        run_code(p, 0, pre_end, R);  // restores spill registers used after the softmax
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) R.acc[j] = __fdiv_rn(sv[q][j], sum);
+      run_code(p, post_begin, p.n_code, R);
+      st4(p, rbase + c, acc4(R, 0), nv);
+    }
+  }
+}
+
+// ========================================================= host compile ===
+static int elt_size(int dtype) { return dtype == FPK_F16 ? 2 : 4; }
+
+struct Compiled {
+  uint8_t code[kMaxCode];
+  float imm[kMaxCode];
+  int n = 0;
+  int softmax_pc = -1;
+  bool uses_tmp = false;
+};
+
+// Compile the op DAG of `d` into accumulator micro-code.
+static int compile_program(const fpk_chain_desc* d, Compiled* out) {
+  const int nin = d->n_inputs;
+  const int nops = d->n_ops;
+  const int nslots = nin + nops;
+  int uses[FPK_CHAIN_MAX_INPUTS + FPK_CHAIN_MAX_OPS] = {0};
+  for (int k = 0; k < nops; ++k) {
+    const fpk_chain_op& op = d->ops[k];
+    uses[op.src_a]++;
+    if (op.opcode == FPK_OP_ADD || op.opcode == FPK_OP_MUL) uses[op.src_b]++;
+  }
+  uses[d->result]++;
+  int slot_tmp[FPK_CHAIN_MAX_INPUTS + FPK_CHAIN_MAX_OPS];
+  for (int s = 0; s < nslots; ++s) slot_tmp[s] = -1;
+  int tmp_slot[kNumTmp] = {-1, -1, -1, -1};
+  int acc = -1;
+  Compiled& c = *out;
+  c.n = 0;
+  auto emit = [&](int code, float imm) -> bool {
+    if (c.n >= kMaxCode) return false;
+    c.code[c.n] = static_cast<uint8_t>(code);
+    c.imm[c.n] = imm;
+    ++c.n;
+    return true;
+  };
+  auto src_code = [&](int slot, int base_in, int base_t) -> int {
+    if (slot < nin) return base_in + slot;
+    if (slot_tmp[slot] >= 0) return base_t + slot_tmp[slot];
+    return -1;
+  };
+  // Save the computed value in acc if it is needed after the current op.
+  auto spill_if_live = [&](int still_needed) -> bool {
+    if (acc < nin || still_needed <= 0 || slot_tmp[acc] >= 0) return true;
+    for (int j = 0; j < kNumTmp; ++j) {
+      if (tmp_slot[j] < 0) {
+        tmp_slot[j] = acc;
+        slot_tmp[acc] = j;
+        c.uses_tmp = true;
+        return emit(C_SAVE_T + j, 0.0f);
+      }
+    }
+    return false;  // more than kNumTmp values live at once
+  };
+  auto release = [&](int slot) {
+    if (slot >= nin && uses[slot] == 0 && slot_tmp[slot] >= 0) {
+      tmp_slot[slot_tmp[slot]] = -1;
+      slot_tmp[slot] = -1;
+    }
+  };
+
+  for (int k = 0; k < nops; ++k) {
+    const fpk_chain_op& op = d->ops[k];
+    const bool binary = op.opcode == FPK_OP_ADD || op.opcode == FPK_OP_MUL;
+    const int a = op.src_a;
+    const int b = binary ? op.src_b : -1;
+    int other = -1;
+    if (acc == a) {
+      other = b;
+    } else if (binary && acc == b) {
+      other = a;
+    } else {
+      if (acc >= 0 && !spill_if_live(uses[acc])) return FPK_ERR_UNSUPPORTED;
+      const int mc = src_code(a, C_MOV_IN, C_MOV_T);
+      if (mc < 0) return FPK_ERR_INVALID;
+      if (!emit(mc, 0.0f)) return FPK_ERR_UNSUPPORTED;
+      acc = a;
+      other = b;
+    }
+    // uses of the acc value after this op
+    const int used_here = (a == acc) + (binary && b == acc);
+    if (!spill_if_live(uses[acc] - used_here)) return FPK_ERR_UNSUPPORTED;
+    int code = -1;
+    float imm = 0.0f;
+    switch (op.opcode) {
+      case FPK_OP_ADD:
+      case FPK_OP_MUL: {
+        const bool add = op.opcode == FPK_OP_ADD;
+        if (other == acc) {
+          code = add ? C_ADD_ACC : C_MUL_ACC;
+        } else {
+          code = src_code(other, add ? C_ADD_IN : C_MUL_IN, add ? C_ADD_T : C_MUL_T);
+          if (code < 0) return FPK_ERR_INVALID;
+        }
+        break;
+      }
+      case FPK_OP_SCALE: code = C_SCALE; imm = op.imm; break;
+      case FPK_OP_RELU: code = C_RELU; break;
+      case FPK_OP_EXP: code = C_EXP; break;
+      case FPK_OP_GELU: code = C_GELU; break;
+      case FPK_OP_SOFTMAX:
+        code = C_SOFTMAX;
+        c.softmax_pc = c.n;
+        break;
+      default: return FPK_ERR_INVALID;
+    }
+    if (!emit(code, imm)) return FPK_ERR_UNSUPPORTED;
+    uses[a]--;
+    if (binary) uses[b]--;
+    release(a);
+    if (binary) release(b);
+    acc = nin + k;
+  }
+  if (acc != d->result) {
+    const int mc = src_code(d->result, C_MOV_IN, C_MOV_T);
+    if (mc < 0) return FPK_ERR_INVALID;
+    if (!emit(mc, 0.0f)) return FPK_ERR_UNSUPPORTED;
+  }
+  return FPK_OK;
+}
+
+static int validate(const fpk_chain_desc* d, int n_inputs) {
+  if (!d || d->size != sizeof(fpk_chain_desc) || d->version != FPK_ABI_VERSION) return FPK_ERR_INVALID;
+  if (d->mode != FPK_CHAIN_FLAT && d->mode != FPK_CHAIN_ROWS) return FPK_ERR_INVALID;
+  if (d->out_dtype != FPK_F16 && d->out_dtype != FPK_F32) return FPK_ERR_INVALID;
+  if (d->rows < 0 || d->cols < 0) return FPK_ERR_INVALID;
+  if (d->n_inputs < 1 || d->n_inputs > FPK_CHAIN_MAX_INPUTS || d->n_inputs != n_inputs) return FPK_ERR_INVALID;
+  if (d->n_ops < 1 || d->n_ops > FPK_CHAIN_MAX_OPS) return FPK_ERR_INVALID;
+  const int nin = d->n_inputs;
+  int softmaxes = 0;
+  for (int i = 0; i < nin; ++i) {
+    if (d->in_dtype[i] != FPK_F16 && d->in_dtype[i] != FPK_F32) return FPK_ERR_INVALID;
+    if (d->in_bcast[i] < FPK_BCAST_FULL || d->in_bcast[i] > FPK_BCAST_SCALAR) return FPK_ERR_INVALID;
+  }
+  for (int k = 0; k < d->n_ops; ++k) {
+    const fpk_chain_op& op = d->ops[k];
+    if (op.opcode < FPK_OP_ADD || op.opcode > FPK_OP_GELU) return FPK_ERR_INVALID;
+    if (op.src_a < 0 || op.src_a >= nin + k) return FPK_ERR_INVALID;
+    if (op.opcode == FPK_OP_ADD || op.opcode == FPK_OP_MUL) {
+      if (op.src_b < 0 || op.src_b >= nin + k) return FPK_ERR_INVALID;
+    }
+    if (op.opcode == FPK_OP_SOFTMAX) ++softmaxes;
+  }
+  if (d->result < 0 || d->result >= nin + d->n_ops) return FPK_ERR_INVALID;
+  if (d->mode == FPK_CHAIN_FLAT && softmaxes != 0) return FPK_ERR_INVALID;
+  if (d->mode == FPK_CHAIN_ROWS) {
+    if (softmaxes != 1) return FPK_ERR_INVALID;
+    if (d->cols > FPK_CHAIN_MAX_ROW_COLS) return FPK_ERR_UNSUPPORTED;
+  }
+  return FPK_OK;
+}
+
+// Opt in once per device to the dynamic shared memory the flat kernel may use.
+template <int NIN, int NT>
+static int launch_flat_n(const Params& p, int grid, int smem, cudaStream_t s) {
+  static std::atomic<int> opted[64];
+  auto k = chain_flat_kernel<NIN, NT>;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FPK_ERR_CUDA;
+  if (!opted[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kStageBudget) != cudaSuccess)
+      return FPK_ERR_CUDA;
+    opted[dev].store(1, std::memory_order_release);
+  }
+  k<<<grid, kFlatThreads, smem, s>>>(p);
+  return cudaGetLastError() == cudaSuccess ? FPK_OK : FPK_ERR_CUDA;
+}
+
+template <int NIN, int TPR, int QPT>
+static int launch_rows_cfg(const Params& p, int num_sms, cudaStream_t s) {
+  int block, grid;
+  if (TPR == 32) {
+    block = 256;
+    const int64_t rows_per_block = block / 32;
+    const int64_t need = (p.rows + rows_per_block - 1) / rows_per_block;
+    grid = static_cast<int>(need < num_sms * 8 ? need : num_sms * 8);
+  } else {
+    block = TPR;
+    grid = static_cast<int>(p.rows < num_sms * 8 ? p.rows : num_sms * 8);
+  }
+  chain_rows_kernel<NIN, TPR, QPT><<<grid, block, 0, s>>>(p);
+  return cudaGetLastError() == cudaSuccess ? FPK_OK : FPK_ERR_CUDA;
+}
+
+template <int NIN>
+static int launch_rows_n(const Params& p, int num_sms, cudaStream_t s) {
+  const int64_t c = p.cols;
+  if (c <= 128) return launch_rows_cfg<NIN, 32, 1>(p, num_sms, s);
+  if (c <= 256) return launch_rows_cfg<NIN, 32, 2>(p, num_sms, s);
+  if (c <= 512) return launch_rows_cfg<NIN, 32, 4>(p, num_sms, s);
+  if (c <= 1024) return launch_rows_cfg<NIN, 32, 8>(p, num_sms, s);
+  if (c <= 2048) return launch_rows_cfg<NIN, 256, 2>(p, num_sms, s);
+  if (c <= 4096) return launch_rows_cfg<NIN, 256, 4>(p, num_sms, s);
+  if (c <= 8192) return launch_rows_cfg<NIN, 256, 8>(p, num_sms, s);
+  return launch_rows_cfg<NIN, 512, 8>(p, num_sms, s);
+}
+
+}  // namespace chain
+
+int launch_chain(const fpk_chain_desc* d, const void* const* inputs, void* out, cudaStream_t stream,
+                 const DeviceInfo& dev) {
+  using namespace chain;
+  if (!d || !inputs || !out) return FPK_ERR_INVALID;
+  int rc = validate(d, d->n_inputs);
+  if (rc != FPK_OK) return rc;
+  Compiled prog;
+  rc = compile_program(d, &prog);
+  if (rc != FPK_OK) return rc;
+
+  const int64_t numel = d->rows * d->cols;
+  if (numel == 0) return FPK_OK;  // nothing to do for an empty tensor
+
+  Params p;
+  std::memset(&p, 0, sizeof(p));
+  p.out = out;
+  p.status = dev.status;
+  p.numel = numel;
+  p.rows = d->rows;
+  p.cols = d->cols;
+  p.out_dtype = d->out_dtype;
+  p.flags = d->flags;
+  p.n_code = prog.n;
+  std::memcpy(p.code, prog.code, sizeof(prog.code));
+  std::memcpy(p.imm, prog.imm, sizeof(prog.imm));
+  const uintptr_t obase = reinterpret_cast<uintptr_t>(out);
+  const int osz = elt_size(d->out_dtype);
+  // vector store of 4 elements: 8 B (f16) or 16 B (f32) aligned, and rows aligned in rows mode
+  p.out_vec = (obase % (4 * osz) == 0) && (d->mode == FPK_CHAIN_FLAT || d->cols % 4 == 0);
+
+  const bool flat = d->mode == FPK_CHAIN_FLAT;
+  for (int i = 0; i < kMaxIn; ++i) p.in[i].mode = M_NONE;
+  int staged_bytes = 0;
+  bool any_col = false, any_row = false;
+  for (int i = 0; i < d->n_inputs; ++i) {
+    Input& in = p.in[i];
+    in.ptr = inputs[i];
+    if (!in.ptr) return FPK_ERR_INVALID;
+    in.dtype = d->in_dtype[i];
+    const int esz = elt_size(in.dtype);
+    const uintptr_t a = reinterpret_cast<uintptr_t>(in.ptr);
+    if (a % esz) return FPK_ERR_ALIGN;
+    const bool vec_ok = a % (4 * esz) == 0;
+    switch (d->in_bcast[i]) {
+      case FPK_BCAST_FULL:
+        if (flat && !(d->flags & FPK_FLAG_NO_STAGING) && a % 16 == 0 &&
+            staged_bytes + kTile * esz <= kMaxStageBytes) {
+          in.mode = M_STAGED;
+          in.smem_off = static_cast<uint32_t>(staged_bytes);
+          staged_bytes += kTile * esz;
+        } else {
+          in.mode = (vec_ok && (flat || d->cols % 4 == 0)) ? M_FULL_VEC : M_FULL_SCALAR;
+        }
+        break;
+      case FPK_BCAST_COL:
+        in.mode = (vec_ok && d->cols % 4 == 0) ? M_COL_VEC : M_COL_SCALAR;
+        any_col |= in.mode == M_COL_VEC;
+        break;
+      case FPK_BCAST_ROW:
+        in.mode = M_ROW;
+        any_row = true;
+        break;
+      default:
+        in.mode = M_SCALAR;
+        break;
+    }
+  }
+
+  if (flat) {
+    p.num_tiles = (numel + kTile - 1) / kTile;
+    p.stage_bytes = staged_bytes;
+    int nstage = staged_bytes ? kStageBudget / staged_bytes : 2;
+    nstage = nstage < 2 ? 2 : (nstage > kMaxStages ? kMaxStages : nstage);
+    p.nstage = nstage;
+    const int64_t max_grid = static_cast<int64_t>(dev.num_sms);
+    const int grid = static_cast<int>(p.num_tiles < max_grid ? p.num_tiles : max_grid);
+    // incremental (row, col) tracking is exact only when quads never straddle rows
+    p.need_idx = (any_col || any_row) && d->cols % 4 == 0;
+    if (p.need_idx) {
+      const int64_t c = d->cols;
+      p.col_step_q = static_cast<uint32_t>((4 * kNCT) % c);
+      p.row_step_q = static_cast<uint32_t>((4 * kNCT) / c);
+      const int64_t tstep = static_cast<int64_t>(grid) * kTile;
+      p.col_step_t = static_cast<uint32_t>(tstep % c);
+      p.row_step_t = tstep / c;
+    }
+    const int smem = nstage * staged_bytes;
+    const bool spills = prog.uses_tmp;
+    switch (d->n_inputs) {
+      case 1: return spills ? launch_flat_n<1, 4>(p, grid, smem, stream) : launch_flat_n<1, 0>(p, grid, smem, stream);
+      case 2: return spills ? launch_flat_n<2, 4>(p, grid, smem, stream) : launch_flat_n<2, 0>(p, grid, smem, stream);
+      case 3: return spills ? launch_flat_n<3, 4>(p, grid, smem, stream) : launch_flat_n<3, 0>(p, grid, smem, stream);
+      case 4: return spills ? launch_flat_n<4, 4>(p, grid, smem, stream) : launch_flat_n<4, 0>(p, grid, smem, stream);
+      default: return spills ? launch_flat_n<8, 4>(p, grid, smem, stream) : launch_flat_n<8, 0>(p, grid, smem, stream);
+    }
+  }
+
+  if (prog.softmax_pc < 0) return FPK_ERR_INVALID;
+  p.n_pre = prog.softmax_pc;
+  for (int pc = prog.softmax_pc + 1; pc < prog.n; ++pc) {
+    const int c = prog.code[pc];
+    if (c < C_SAVE_T || (c >= C_ADD_IN && c < C_ADD_ACC) || (c >= C_MUL_IN && c < C_MUL_ACC)) p.post_reload = 1;
+  }
+  switch (d->n_inputs) {
+    case 1: return launch_rows_n<1>(p, dev.num_sms, stream);
+    case 2: return launch_rows_n<2>(p, dev.num_sms, stream);
+    case 3: case 4: return launch_rows_n<4>(p, dev.num_sms, stream);
+    default: return launch_rows_n<8>(p, dev.num_sms, stream);
+  }
+}
+
+}  // namespace fpk

@@ -1,0 +1,228 @@
+"""Tensor-level calls into libfpkern: descriptors in, kernels enqueued on torch's stream.
+
+Descriptor format (what a plan step carries in ``attrs["desc"]``)::
+
+    chain:     {"op": "chain", "mode": "flat" | "rows",
+                "inputs": [{"dtype": "f16", "bcast": "full" | "col" | "row" | "scalar"}, ...],
+                "ops": [{"op": "add", "a": 0, "b": 1}, {"op": "scale", "a": 2, "imm": 0.5}, ...],
+                "result": <slot>}
+    attention: {"op": "attention", "scale": <float>, "head_dim": <16|32|64|128>}
+
+Slots ``0..n_inputs-1`` are the step's operands in order; slot ``n_inputs + k`` is
+the result of op ``k``.  All math is f32 with one rounding at the store.
+PyTorch supplies device memory and the current CUDA stream only; every fused
+step runs in ``libfpkern.so`` and there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from collections import OrderedDict
+from typing import Any, Mapping, Sequence
+
+import torch
+
+from . import _lib
+
+_TORCH_DT = {torch.float32: _lib.FPK_F32, torch.float16: _lib.FPK_F16}
+_NAME_DT = {"f32": _lib.FPK_F32, "f16": _lib.FPK_F16}
+_DT_NAME = {torch.float32: "f32", torch.float16: "f16"}
+
+_cache_lock = threading.Lock()
+_desc_cache: "OrderedDict[tuple, tuple]" = OrderedDict()
+_CACHE_MAX = 256
+
+
+def _stream_handle(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def require_cuda(t: torch.Tensor, what: str) -> None:
+    if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
+        raise RuntimeError(f"{what}: fused steps run only in libfpkern.so on a CUDA device "
+                           f"(got {getattr(t, 'device', type(t))}); there is no CPU path")
+
+
+def _bcast_of(t: torch.Tensor, rows: int, cols: int, declared: str | None) -> str:
+    n = t.numel()
+    if declared is not None:
+        want = {"full": rows * cols, "col": cols, "row": rows, "scalar": 1}[declared]
+        if n != want:
+            raise ValueError(f"operand with {n} elements does not match broadcast '{declared}' "
+                             f"of a [{rows}, {cols}] chain")
+        return declared
+    if n == rows * cols:
+        return "full"
+    if n == cols:
+        return "col"
+    if n == rows:
+        return "row"
+    if n == 1:
+        return "scalar"
+    raise ValueError(f"operand with {n} elements cannot broadcast onto [{rows}, {cols}]")
+
+
+def build_chain_desc(desc: Mapping[str, Any], rows: int, cols: int, in_dtypes: Sequence[int],
+                     bcasts: Sequence[str], out_dtype: int, flags: int = 0) -> _lib.ChainDesc:
+    """Fill the C descriptor for one chain launch (validated again by the library)."""
+    ops = desc["ops"]
+    n_in = len(in_dtypes)
+    if not 1 <= n_in <= _lib.FPK_CHAIN_MAX_INPUTS:
+        raise ValueError(f"chain needs 1..{_lib.FPK_CHAIN_MAX_INPUTS} inputs, got {n_in}")
+    if not 1 <= len(ops) <= _lib.FPK_CHAIN_MAX_OPS:
+        raise ValueError(f"chain needs 1..{_lib.FPK_CHAIN_MAX_OPS} ops, got {len(ops)}")
+    d = _lib.ChainDesc()
+    d.size = ctypes.sizeof(_lib.ChainDesc)
+    d.version = _lib.FPK_ABI_VERSION
+    d.mode = _lib.FPK_CHAIN_ROWS if desc.get("mode") == "rows" else _lib.FPK_CHAIN_FLAT
+    d.out_dtype = out_dtype
+    d.rows = rows
+    d.cols = cols
+    d.n_inputs = n_in
+    d.n_ops = len(ops)
+    d.result = int(desc["result"])
+    d.flags = flags
+    for i in range(n_in):
+        d.in_dtype[i] = in_dtypes[i]
+        d.in_bcast[i] = _lib.BCAST[bcasts[i]]
+    for k, op in enumerate(ops):
+        name = op["op"]
+        if name not in _lib.OPCODES:
+            raise ValueError(f"unsupported op in chain: {name}")
+        d.ops[k].opcode = _lib.OPCODES[name]
+        d.ops[k].src_a = int(op["a"])
+        d.ops[k].src_b = int(op.get("b", -1))
+        d.ops[k].imm = float(op.get("imm", 0.0))
+    return d
+
+
+def _cached_chain_desc(desc, rows, cols, in_dtypes, bcasts, out_dtype, flags):
+    key = (id(desc), rows, cols, tuple(in_dtypes), tuple(bcasts), out_dtype, flags)
+    with _cache_lock:
+        hit = _desc_cache.get(key)
+        if hit is not None and hit[0] is desc:
+            _desc_cache.move_to_end(key)
+            return hit[1]
+    c = build_chain_desc(desc, rows, cols, in_dtypes, bcasts, out_dtype, flags)
+    with _cache_lock:
+        _desc_cache[key] = (desc, c)  # holding `desc` keeps its id unique while cached
+        if len(_desc_cache) > _CACHE_MAX:
+            _desc_cache.popitem(last=False)
+    return c
+
+
+def chain(inputs: Sequence[torch.Tensor], desc: Mapping[str, Any], out_shape, out_dtype: torch.dtype,
+          out: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
+    """Run one fused chain; ``out_shape`` is the step's result shape ([..., cols])."""
+    lib = _lib.load()
+    out_shape = [int(s) for s in out_shape]
+    if not inputs:
+        raise ValueError("chain needs at least one input")
+    for t in inputs:
+        require_cuda(t, "chain")
+    dev = inputs[0].device
+    cols = out_shape[-1] if out_shape else 1
+    numel = 1
+    for s in out_shape:
+        numel *= s
+    rows = numel // cols if cols else 0
+    declared = [spec.get("bcast") for spec in desc.get("inputs", [])] or [None] * len(inputs)
+    if len(declared) != len(inputs):
+        raise ValueError(f"descriptor lists {len(declared)} inputs, step has {len(inputs)}")
+    ins = []
+    bcasts = []
+    for t, dec in zip(inputs, declared):
+        if t.dtype not in _TORCH_DT:
+            raise ValueError(f"unsupported dtype {t.dtype}")
+        if t.device != dev:
+            raise ValueError("all chain operands must be on one device")
+        bcasts.append(_bcast_of(t, rows, cols, dec))
+        ins.append(t.contiguous())
+    if out is None:
+        out = torch.empty(out_shape, dtype=out_dtype, device=dev)
+    elif not out.is_contiguous() or list(out.shape) != out_shape or out.dtype != out_dtype:
+        raise ValueError("out must be a contiguous tensor of the step's shape and dtype")
+    c = _cached_chain_desc(desc, rows, cols, [_TORCH_DT[t.dtype] for t in ins], bcasts,
+                           _TORCH_DT[out_dtype], flags)
+    ptrs = (ctypes.c_void_p * len(ins))(*[t.data_ptr() for t in ins])
+    with torch.cuda.device(dev):
+        rc = lib.fpk_chain_fwd(ctypes.byref(c), ptrs, len(ins), ctypes.c_void_p(out.data_ptr()),
+                               _stream_handle(dev))
+    _lib.check(rc, "fpk_chain_fwd")
+    return out
+
+
+def _bhsd(t: torch.Tensor):
+    """(B, H, S, D, strides[b, h, s]) of a [..., S, D] tensor with a unit D stride."""
+    if t.dim() < 3:
+        raise ValueError("attention tensors must have rank >= 3 ([batch..., S, D])")
+    if t.stride(-1) != 1:
+        t = t.contiguous()
+    S, D = t.shape[-2], t.shape[-1]
+    if t.dim() == 3:
+        B, H = 1, t.shape[0]
+        st = (t.shape[0] * t.stride(0), t.stride(0), t.stride(1))
+    else:
+        lead = t.shape[:-3]
+        B = 1
+        for s in lead:
+            B *= s
+        H = t.shape[-3]
+        # leading dims must flatten to one stride
+        if t.dim() > 4:
+            exp = t.stride(-4)
+            for i in range(t.dim() - 5, -1, -1):
+                exp *= t.shape[i + 1]
+                if t.stride(i) != exp:
+                    t = t.contiguous()
+                    break
+        b_stride = t.stride(-4) if t.dim() >= 4 else H * t.stride(-3)
+        st = (b_stride, t.stride(-3), t.stride(-2))
+    return t, B, H, S, D, st
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+              out: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
+    """``softmax(scale * q @ k^T) @ v`` over ``[..., S, D]`` (self-attention shapes)."""
+    lib = _lib.load()
+    for t in (q, k, v):
+        require_cuda(t, "attention")
+    if not (q.shape == k.shape == v.shape) or not (q.dtype == k.dtype == v.dtype):
+        raise ValueError("q, k, v must share one shape and dtype (FusedAttentionOp contract)")
+    if q.dtype not in _TORCH_DT:
+        raise ValueError(f"unsupported dtype {q.dtype}")
+    q, B, H, S, D, qs = _bhsd(q)
+    k, _, _, _, _, ks = _bhsd(k)
+    v, _, _, _, _, vs = _bhsd(v)
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    elif out.shape != q.shape or out.dtype != q.dtype:
+        raise ValueError("out must match q's shape and dtype")
+    out_t, _, _, _, _, os_ = _bhsd(out)
+    if out_t.data_ptr() != out.data_ptr():
+        raise ValueError("out must have a unit stride in its last dim and flattenable batch dims")
+    d = _lib.AttnDesc()
+    d.size = ctypes.sizeof(_lib.AttnDesc)
+    d.version = _lib.FPK_ABI_VERSION
+    d.dtype = _TORCH_DT[q.dtype]
+    d.head_dim = D
+    d.batch, d.heads, d.seq_len = B, H, S
+    d.scale = float(scale)
+    d.flags = flags
+    for i in range(3):
+        d.q_strides[i], d.k_strides[i], d.v_strides[i], d.o_strides[i] = qs[i], ks[i], vs[i], os_[i]
+    with torch.cuda.device(q.device):
+        rc = lib.fpk_attention_fwd(ctypes.byref(d), ctypes.c_void_p(q.data_ptr()),
+                                   ctypes.c_void_p(k.data_ptr()), ctypes.c_void_p(v.data_ptr()),
+                                   ctypes.c_void_p(out.data_ptr()), _stream_handle(q.device))
+    _lib.check(rc, "fpk_attention_fwd")
+    return out
+
+
+def poll_status(device: torch.device | int | None = None) -> int:
+    """Synchronise the current stream and return/clear the device status word."""
+    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index or 0))
+    return int(lib.fpk_poll_status(dev.index, _stream_handle(dev)))
