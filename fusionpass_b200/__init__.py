@@ -5,13 +5,18 @@ Public API mirrors the reference package ``fusionpass``: ``execute_plan``,
 fused steps run in ``libfpkern.so`` (C ABI in ``include/fpkern.h``).
 """
 
+from .api import CompiledModel, compile_model
 from .bench import BenchResult, UnverifiedSpeedupError, benchmark
 from .kernels import DescriptorWriter, KernelTable, launch_step, load_kernels
+from .planner import UnsupportedOp
 from .runtime import execute_plan
 from .validate import validate_plan
 from .verify import EquivalenceError, VerifyReport, assert_equivalent, verify_equivalence
 
 __all__ = [
+    "compile_model",
+    "CompiledModel",
+    "UnsupportedOp",
     "execute_plan",
     "validate_plan",
     "launch_step",

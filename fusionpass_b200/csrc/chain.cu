@@ -371,6 +371,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) chain_flat_kernel(const __gri
         if ((p.flags & FPK_FLAG_TEST_TIMEOUT) && li == 0) continue;  // withheld on purpose
         const int64_t e0 = tile * kTile;
         const bool whole = e0 + kTile <= p.numel;
+        last_li[s] = li;  // the newest phase of this stage (copy or plain arrive)
         if (whole && p.stage_bytes > 0) {
           mbar_arrive_expect_tx(&full_bar[s], static_cast<uint32_t>(p.stage_bytes));
           uint8_t* dst = smem + static_cast<size_t>(s) * p.stage_bytes;
@@ -383,12 +384,14 @@ __global__ void __launch_bounds__(kFlatThreads, 1) chain_flat_kernel(const __gri
                        static_cast<uint32_t>(kTile * esz), &full_bar[s], pol);
             }
           }
-          last_li[s] = li;
         } else {
           mbar_arrive(&full_bar[s]);
         }
       }
-      // Drain: no bulk copy may still be in flight when the CTA exits.
+      // Drain: no bulk copy may still be in flight when the CTA exits.  Phases of
+      // one barrier complete in order, so waiting for the newest phase of every
+      // stage covers all copies issued to it (a parity taken from an older phase
+      // could alias a phase two steps later).
       for (int s = 0; s < nstage; ++s) {
         if (last_li[s] < 0) continue;
         const uint32_t par = static_cast<uint32_t>(last_li[s] / nstage) & 1u;
@@ -791,15 +794,16 @@ static int launch_rows_n(const Params& p, int num_sms, cudaStream_t s) {
 int launch_chain(const fpk_chain_desc* d, const void* const* inputs, void* out, cudaStream_t stream,
                  const DeviceInfo& dev) {
   using namespace chain;
-  if (!d || !inputs || !out) return FPK_ERR_INVALID;
+  if (!d || !inputs) return FPK_ERR_INVALID;
   int rc = validate(d, d->n_inputs);
   if (rc != FPK_OK) return rc;
+  const int64_t numel = d->rows * d->cols;
+  if (numel == 0) return FPK_OK;  // an empty tensor: nothing to launch (its pointers may be null)
+  if (!out) return FPK_ERR_INVALID;
   Compiled prog;
   rc = compile_program(d, &prog);
   if (rc != FPK_OK) return rc;
 
-  const int64_t numel = d->rows * d->cols;
-  if (numel == 0) return FPK_OK;  // nothing to do for an empty tensor
 
   Params p;
   std::memset(&p, 0, sizeof(p));

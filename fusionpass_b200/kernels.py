@@ -247,6 +247,6 @@ def launch_step(step: dict, ops: Sequence[Any], kernels):
     else:
         if len(ops) != 3:
             raise ValueError("attention needs exactly 3 operands")
-        q, k, v = (o.contiguous() for o in ops)
+        q, k, v = ops  # strided [B, H, S, D] views go straight to the strided TMA maps
         launch_attention(q, k, v, out, scale=a["scale"])
     return out

@@ -38,6 +38,18 @@ def _run_torch(step: dict, ops: list) -> torch.Tensor:
         return torch.matmul(ops[0], ops[1])
     if op == "transpose":
         return ops[0].transpose(-1, -2)
+    # extension steps (planner extensions=True)
+    if op == "gelu":
+        return torch.nn.functional.gelu(ops[0])
+    if op == "linear":
+        return torch.nn.functional.linear(ops[0], ops[1])
+    if op == "layer_norm":
+        w, b = (ops[1], ops[2]) if len(ops) == 3 else (None, None)
+        return torch.nn.functional.layer_norm(ops[0], attrs["normalized_shape"], w, b, attrs["eps"])
+    if op == "reshape":
+        return ops[0].reshape(attrs["shape"])
+    if op == "permute":
+        return ops[0].permute(*attrs["dims"])
     raise ValueError(f"unknown torch op in plan: {op}")
 
 

@@ -12,6 +12,8 @@ from __future__ import annotations
 
 DTYPES = {"f16", "f32"}
 TORCH_OPS = {"add", "mul", "scale", "relu", "exp", "softmax", "matmul", "transpose"}
+# unfused steps the planner emits only with extensions=True (BERT-style blocks)
+EXTENSION_TORCH_OPS = {"gelu", "linear", "layer_norm", "reshape", "permute"}
 LAUNCHES = {"flat", "rows", "attention"}
 _CHAIN_OPS = {"add", "mul", "scale", "relu", "exp", "softmax", "gelu"}
 
@@ -71,7 +73,7 @@ def validate_plan(plan: dict) -> None:
             raise ValueError(f"step {i}: bad dtype")
         kind = st.get("kind")
         if kind == "torch":
-            if st.get("op") not in TORCH_OPS:
+            if st.get("op") not in TORCH_OPS | EXTENSION_TORCH_OPS:
                 raise ValueError(f"step {i}: unknown torch op '{st.get('op')}'")
         elif kind == "triton":
             if st.get("launch") not in LAUNCHES or not st.get("kernel"):

@@ -18,6 +18,14 @@ from tests import _golden
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(autouse=True)
+def _device_status_clean(request):
+    """Every kernel of every test must leave the device status word clean."""
+    yield
+    if "timeout" not in request.node.name:
+        assert fpkern.poll_status() == 0, "a kernel recorded a device-side error"
+
 TOL = {"f32": (1e-5, 1e-5), "f16": (2e-3, 1e-2)}
 _DT = {"f32": torch.float32, "f16": torch.float16}
 
