@@ -364,27 +364,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t sr[128];
         tmem_ld_x128(tS, sr);
         const int valid = S - j * kBN;  // > 0; < 128 only on the last tile
-        float mx = -INFINITY;
+        // row max (or min for a negative scale) over 8 independent lanes of ILP
+        float m8[8];
+        const float init = k2 >= 0.0f ? -INFINITY : INFINITY;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = init;
         if (valid >= kBN) {
           if (k2 >= 0.0f) {
 #pragma unroll
-            for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+            for (int c = 0; c < kBN; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
           } else {
-            mx = INFINITY;
 #pragma unroll
-            for (int c = 0; c < kBN; ++c) mx = fminf(mx, __uint_as_float(sr[c]));
+            for (int c = 0; c < kBN; ++c) m8[c & 7] = fminf(m8[c & 7], __uint_as_float(sr[c]));
           }
         } else {
           if (k2 >= 0.0f) {
 #pragma unroll
             for (int c = 0; c < kBN; ++c)
-              if (c < valid) mx = fmaxf(mx, __uint_as_float(sr[c]));
+              if (c < valid) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
           } else {
-            mx = INFINITY;
 #pragma unroll
             for (int c = 0; c < kBN; ++c)
-              if (c < valid) mx = fminf(mx, __uint_as_float(sr[c]));
+              if (c < valid) m8[c & 7] = fminf(m8[c & 7], __uint_as_float(sr[c]));
           }
+        }
+        float mx;
+        if (k2 >= 0.0f) {
+          mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        } else {
+          mx = fminf(fminf(fminf(m8[0], m8[1]), fminf(m8[2], m8[3])), fminf(fminf(m8[4], m8[5]), fminf(m8[6], m8[7])));
         }
         mx *= k2;  // row max of the log2-scaled scores
         if (j == 0) {
@@ -409,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         const float neg_m = -m_run;
-        float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        float ls[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
         uint32_t pk[64];
 #pragma unroll
         for (int c = 0; c < kBN; c += 2) {
@@ -419,10 +427,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             p0 = c < valid ? p0 : 0.0f;
             p1 = c + 1 < valid ? p1 : 0.0f;
           }
-          ls[(c >> 1) & 3] += p0 + p1;
+          ls[(c >> 1) & 7] += p0;
+          ls[(c >> 1) & 7] += p1;
           pk[c >> 1] = pack_half2(p0, p1);
         }
-        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
         tmem_st_x64(tS, pk);
         tmem_st_wait();
         tc_fence_before();

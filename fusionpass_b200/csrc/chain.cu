@@ -99,7 +99,12 @@ struct Params {
 };
 
 // ------------------------------------------------------- f32 element ops ---
-__device__ __forceinline__ float op_relu(float x) { return x != x ? x : fmaxf(x, 0.0f); }
+// max(x, 0) that propagates NaN like the reference's numpy maximum (one instruction)
+__device__ __forceinline__ float op_relu(float x) {
+  float y;
+  asm("max.NaN.f32 %0, %1, 0f00000000;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ float op_gelu(float x) {
   const float t = __fmul_rn(x, 0.70710678118654752f);
@@ -592,6 +597,347 @@ __global__ void __launch_bounds__(TPR > 32 ? TPR : 256) chain_rows_kernel(const 
   }
 }
 
+// ========================================================= row-tiled flat ===
+// The common shape of a flat chain: inputs are full [rows, cols] tensors and
+// per-column vectors, cols % 8 == 0, one dtype throughout, no spill registers.
+// Inputs are put in canonical order (full ones first, then per-column ones) so
+// that every micro-op knows the class of its operand at compile time.
+// Each consumer thread owns fixed 8-column vectors and keeps only the running
+// value (4 vectors = 32 elements, as 16 packed f32 pairs) in registers; full
+// operands are read from the TMA stage with 32-bit shared addresses, per-column
+// operands from an f32 copy in shared memory whose addresses are fixed per
+// thread.  add / mul / scale run as packed add.rn.f32x2 / mul.rn.f32x2 (per
+// lane identical to the scalar round-to-nearest ops).  TMA streams whole row
+// blocks: one bulk copy per full input per stage.
+constexpr int kTV = 32;               // elements per dispatch (4 vectors of 8)
+constexpr int kTP = kTV / 2;          // packed f32 pairs per dispatch
+constexpr int kTConsumers = 512;      // 16 consumer warps + 1 producer warp (<= 96 registers)
+constexpr int kTThreads = kTConsumers + 32;
+constexpr int kTStageBudget = 128 * 1024;
+constexpr int kTColBudget = 64 * 1024;  // f32 copies of the per-column operands
+constexpr int kTMaxCode = 16;         // program held in two 64-bit registers
+
+struct TParams {
+  const void* in_ptr[kMaxIn];    // canonical order: full inputs, then per-column inputs
+  void* out;
+  int* status;
+  int64_t rows, cols;
+  int64_t num_blocks;            // row blocks of stage_rows rows
+  int32_t cv;                    // cols / 8
+  int32_t teff;                  // consumer threads in use
+  int32_t rps;                   // rows per thread step (one vector per row per thread: teff / cv)
+  int32_t stage_rows;
+  int32_t dispatches;            // dispatches per stage
+  int32_t in_bytes;              // bytes of one full input inside a stage
+  int32_t col_pad;               // floats per per-column operand in shared memory (>= cols)
+  int32_t col_pad_bytes;         // padding after the stages for reads of masked slots
+  int32_t stage_bytes;
+  int32_t nstage;
+  int32_t n_code;
+  uint32_t flags;
+  uint64_t code_lo, code_hi;     // micro-ops 0..7 and 8..15, 8 bits each
+  float imm[kTMaxCode];
+};
+
+// ---- packed f32 pairs
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t h2_to_f2(uint32_t h) {
+  const float2 f = unpack_half2(h);
+  return f2_pack(f.x, f.y);
+}
+
+// 8 elements at a 32-bit shared address -> 4 packed pairs
+template <int DT>
+__device__ __forceinline__ void t_lds8(uint32_t addr, uint64_t* v) {
+  uint32_t a, b, c, d;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "r"(addr));
+  if constexpr (DT == FPK_F16) {
+    v[0] = h2_to_f2(a);
+    v[1] = h2_to_f2(b);
+    v[2] = h2_to_f2(c);
+    v[3] = h2_to_f2(d);
+  } else {
+    uint32_t e, f, g, h;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(e), "=r"(f), "=r"(g), "=r"(h) : "r"(addr + 16));
+    v[0] = (static_cast<uint64_t>(b) << 32) | a;
+    v[1] = (static_cast<uint64_t>(d) << 32) | c;
+    v[2] = (static_cast<uint64_t>(f) << 32) | e;
+    v[3] = (static_cast<uint64_t>(h) << 32) | g;
+  }
+}
+
+// 8 f32 at a 32-bit shared address -> 4 packed pairs
+__device__ __forceinline__ void t_lds8f(uint32_t addr, uint64_t* v) {
+  asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(v[0]), "=l"(v[1]) : "r"(addr));
+  asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(v[2]), "=l"(v[3]) : "r"(addr + 16));
+}
+
+// Addressing of the 4 slots of a dispatch: slot q is vector (q % NV) of row
+// (q / NV) of the thread's row step, so every address is affine in q with
+// warp-uniform strides and only one base offset per dispatch is kept.
+template <int NF, int NC>
+struct TCtx {
+  uint32_t in_base[NF];              // shared address of full input i in the current stage
+  uint32_t col[NC > 0 ? NC : 1];     // shared address of this thread's first column vector in input j
+  uint32_t row_stride;               // bytes between the rows of consecutive slots (rps rows)
+  uint32_t vec_stride;               // bytes between vectors of consecutive slots (teff vectors)
+  uint32_t col_stride;               // bytes between per-column vectors of consecutive slots
+};
+
+// acc (op) operand I (compile-time, canonical order) for the 4 slots at offset e0
+template <int DT, int NF, int NC, int NV, int I, int OP>
+__device__ __forceinline__ void t_op_in(const TCtx<NF, NC>& cx, uint32_t e0, uint64_t* acc) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint64_t v[4];
+    if constexpr (I < NF) {
+      t_lds8<DT>(cx.in_base[I < NF ? I : 0] + e0 + (q / NV) * cx.row_stride + (q % NV) * cx.vec_stride, v);
+    } else {
+      t_lds8f(cx.col[I < NF ? 0 : I - NF] + (q % NV) * cx.col_stride, v);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint64_t& a = acc[q * 4 + k];
+      if constexpr (OP == 0) a = v[k];
+      else if constexpr (OP == 1) a = f2_add(a, v[k]);
+      else a = f2_mul(a, v[k]);
+    }
+  }
+}
+
+template <int DT, int NF, int NC, int NV>
+__device__ __forceinline__ void run_tiled(const TParams& p, const TCtx<NF, NC>& cx, uint32_t e0, uint64_t* acc) {
+  uint64_t lo = p.code_lo, hi = p.code_hi;
+  // the first micro-op moves an operand into acc; every later one updates acc in place
+  switch (static_cast<int>(lo & 0xffu)) {
+#define FPK_TMOV(I) \
+  case C_MOV_IN + I: \
+    if constexpr (I < NF + NC) t_op_in<DT, NF, NC, NV, (I < NF + NC ? I : 0), 0>(cx, e0, acc); \
+    break;
+    FPK_TMOV(0) FPK_TMOV(1) FPK_TMOV(2) FPK_TMOV(3) FPK_TMOV(4)
+#undef FPK_TMOV
+    default: break;
+  }
+  lo = (lo >> 8) | (hi << 56);
+  hi >>= 8;
+#pragma unroll 1
+  for (int pc = 1; pc < p.n_code; ++pc) {
+    const int c = static_cast<int>(lo & 0xffu);
+    lo = (lo >> 8) | (hi << 56);
+    hi >>= 8;
+    switch (c) {
+#define FPK_TIN(I)                                                                         \
+  case C_ADD_IN + I:                                                                       \
+    if constexpr (I < NF + NC) t_op_in<DT, NF, NC, NV, (I < NF + NC ? I : 0), 1>(cx, e0, acc);  \
+    break;                                                                                 \
+  case C_MUL_IN + I:                                                                       \
+    if constexpr (I < NF + NC) t_op_in<DT, NF, NC, NV, (I < NF + NC ? I : 0), 2>(cx, e0, acc);  \
+    break;
+      FPK_TIN(0) FPK_TIN(1) FPK_TIN(2) FPK_TIN(3) FPK_TIN(4)
+#undef FPK_TIN
+      case C_ADD_ACC:
+#pragma unroll
+        for (int k = 0; k < kTP; ++k) acc[k] = f2_add(acc[k], acc[k]);
+        break;
+      case C_MUL_ACC:
+#pragma unroll
+        for (int k = 0; k < kTP; ++k) acc[k] = f2_mul(acc[k], acc[k]);
+        break;
+      case C_SCALE: {
+        const float sc = p.imm[pc];
+        const uint64_t s2 = f2_pack(sc, sc);
+#pragma unroll
+        for (int k = 0; k < kTP; ++k) acc[k] = f2_mul(acc[k], s2);
+        break;
+      }
+      case C_RELU:
+#pragma unroll
+        for (int k = 0; k < kTP; ++k) {
+          const float2 f = f2_unpack(acc[k]);
+          acc[k] = f2_pack(op_relu(f.x), op_relu(f.y));
+        }
+        break;
+      case C_EXP:
+#pragma unroll
+        for (int k = 0; k < kTP; ++k) {
+          const float2 f = f2_unpack(acc[k]);
+          acc[k] = f2_pack(expf(f.x), expf(f.y));
+        }
+        break;
+      case C_GELU:
+#pragma unroll
+        for (int k = 0; k < kTP; ++k) {
+          const float2 f = f2_unpack(acc[k]);
+          acc[k] = f2_pack(op_gelu(f.x), op_gelu(f.y));
+        }
+        break;
+      default:
+        break;
+    }
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void t_st8(void* base, int64_t idx, const uint64_t* v) {
+  if constexpr (DT == FPK_F16) {
+    uint4 u;
+    const float2 a = f2_unpack(v[0]), b = f2_unpack(v[1]), c = f2_unpack(v[2]), d = f2_unpack(v[3]);
+    u.x = pack_half2(a.x, a.y);
+    u.y = pack_half2(b.x, b.y);
+    u.z = pack_half2(c.x, c.y);
+    u.w = pack_half2(d.x, d.y);
+    *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(base) + idx) = u;
+  } else {
+    ulonglong2* q = reinterpret_cast<ulonglong2*>(reinterpret_cast<float*>(base) + idx);
+    q[0] = make_ulonglong2(v[0], v[1]);
+    q[1] = make_ulonglong2(v[2], v[3]);
+  }
+}
+
+// NV = 8-column vectors a thread owns per row (1, 2 or 4); slot s of a dispatch
+// is vector (s % NV) of row (s / NV) of the thread's current row step.
+template <int DT, int NF, int NC, int NV>
+__global__ void __launch_bounds__(kTThreads, 1) chain_tiled_kernel(const __grid_constant__ TParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full_bar[kMaxStages];
+  __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+  __shared__ volatile int abort_flag;
+  constexpr int esz = DT == FPK_F16 ? 2 : 4;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int ncw = (p.teff + 31) >> 5;  // consumer warps; the producer is warp ncw
+  const int nstage = p.nstage;
+  // column area after the stages and the read-overrun padding (16-byte aligned)
+  float* cols = reinterpret_cast<float*>(
+      smem + ((static_cast<size_t>(nstage) * p.stage_bytes + p.col_pad_bytes + 15) & ~static_cast<size_t>(15)));
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nstage; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], ncw);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  // per-column operands -> f32 in shared memory (all threads of the CTA help); the
+  // padding past cols (read by masked slots only) is zero-filled
+#pragma unroll
+  for (int j = 0; j < NC; ++j)
+    for (int c = threadIdx.x; c < p.col_pad; c += blockDim.x)
+      cols[j * p.col_pad + c] = c < p.cols ? ld1(p.in_ptr[NF + j], c, DT) : 0.0f;
+  __syncthreads();
+  const uint64_t limit = (p.flags & FPK_FLAG_TEST_TIMEOUT) ? kTestWaitLimitNs : kWaitLimitNs;
+  const int64_t G = gridDim.x;
+  const int64_t C = p.cols;
+  const int64_t row_bytes = C * esz;
+
+  if (warp == ncw) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      int64_t last_li[kMaxStages];
+      for (int s = 0; s < kMaxStages; ++s) last_li[s] = -1;
+      int64_t li = 0;
+      for (int64_t blk = blockIdx.x; blk < p.num_blocks; blk += G, ++li) {
+        const int s = static_cast<int>(li % nstage);
+        const uint32_t r = static_cast<uint32_t>(li / nstage);
+        if (!mbar_wait(&empty_bar[s], (r & 1u) ^ 1u, &abort_flag, p.status, limit)) break;
+        if ((p.flags & FPK_FLAG_TEST_TIMEOUT) && li == 0) continue;  // withheld on purpose
+        last_li[s] = li;
+        const int64_t r0 = blk * p.stage_rows;
+        const int64_t nr = (p.rows - r0) < p.stage_rows ? (p.rows - r0) : p.stage_rows;
+        const uint32_t bytes = static_cast<uint32_t>(nr * row_bytes);
+        mbar_arrive_expect_tx(&full_bar[s], bytes * NF);
+        uint8_t* dst = smem + static_cast<size_t>(s) * p.stage_bytes;
+#pragma unroll
+        for (int i = 0; i < NF; ++i)
+          bulk_g2s(dst + i * p.in_bytes, reinterpret_cast<const uint8_t*>(p.in_ptr[i]) + r0 * row_bytes, bytes,
+                   &full_bar[s], pol);
+      }
+      for (int s = 0; s < nstage; ++s) {  // newest phase of every stage: no copy left in flight
+        if (last_li[s] < 0) continue;
+        const uint32_t par = static_cast<uint32_t>(last_li[s] / nstage) & 1u;
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full_bar[s], par)) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            record_status(p.status, FPK_ERR_TIMEOUT);
+            break;
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  const int t = threadIdx.x;
+  const bool active = t < p.teff;
+  const int my_row0 = NV == 1 ? t / p.cv : 0;
+  const int my_vec0 = NV == 1 ? t % p.cv : t;
+  constexpr int kRD = 4 / NV;  // rows per dispatch of one thread
+  const int rows_per_dispatch = kRD * p.rps;
+  const uint32_t smem0 = smem_u32(smem);
+  TCtx<NF, NC> cx;
+  cx.row_stride = static_cast<uint32_t>(p.rps * C * esz);
+  cx.vec_stride = static_cast<uint32_t>(p.teff * 8 * esz);
+  cx.col_stride = static_cast<uint32_t>(p.teff * 8 * 4);
+#pragma unroll
+  for (int j = 0; j < NC; ++j) cx.col[j] = smem_u32(cols) + static_cast<uint32_t>((j * p.col_pad + my_vec0 * 8) * 4);
+  uint32_t vec_ok = 0;  // bit q: the vector of slot q lies inside the row
+#pragma unroll
+  for (int q = 0; q < 4; ++q) vec_ok |= (my_vec0 + (q % NV) * p.teff < p.cv ? 1u : 0u) << q;
+  const uint32_t e_thread = static_cast<uint32_t>((my_row0 * C + my_vec0 * 8) * esz);
+  const uint32_t e_dispatch = static_cast<uint32_t>(rows_per_dispatch * C * esz);
+  uint64_t acc[kTP];
+
+  int64_t li = 0;
+  for (int64_t blk = blockIdx.x; blk < p.num_blocks; blk += G, ++li) {
+    const int s = static_cast<int>(li % nstage);
+    const uint32_t r = static_cast<uint32_t>(li / nstage);
+    if (!mbar_wait(&full_bar[s], r & 1u, &abort_flag, p.status, limit)) break;
+    const int64_t r0 = blk * p.stage_rows;
+    const int nr = static_cast<int>((p.rows - r0) < p.stage_rows ? (p.rows - r0) : p.stage_rows);
+    const uint32_t stage0 = smem0 + static_cast<uint32_t>(s * p.stage_bytes);
+#pragma unroll
+    for (int i = 0; i < NF; ++i) cx.in_base[i] = stage0 + static_cast<uint32_t>(i * p.in_bytes);
+    char* out_blk = reinterpret_cast<char*>(p.out) + r0 * row_bytes;
+    if (active) {
+#pragma unroll 1
+      for (int u = 0; u < p.dispatches; ++u) {
+        const uint32_t e0 = e_thread + static_cast<uint32_t>(u) * e_dispatch;
+        run_tiled<DT, NF, NC, NV>(p, cx, e0, acc);
+        const int row0 = u * rows_per_dispatch + my_row0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (((vec_ok >> q) & 1u) && row0 + (q / NV) * p.rps < nr)
+            t_st8<DT>(out_blk + e0 + (q / NV) * cx.row_stride + (q % NV) * cx.vec_stride, 0, &acc[q * 4]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[s]);
+  }
+}
+
 // ========================================================= host compile ===
 static int elt_size(int dtype) { return dtype == FPK_F16 ? 2 : 4; }
 
@@ -789,6 +1135,150 @@ static int launch_rows_n(const Params& p, int num_sms, cudaStream_t s) {
   return launch_rows_cfg<NIN, 512, 8>(p, num_sms, s);
 }
 
+template <int DT, int NF, int NC, int NV>
+static int launch_tiled_v(const TParams& p, int grid, int block, int smem, cudaStream_t s) {
+  static std::atomic<int> opted[64];
+  auto k = chain_tiled_kernel<DT, NF, NC, NV>;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FPK_ERR_CUDA;
+  if (!opted[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kTStageBudget + kTColBudget) !=
+        cudaSuccess)
+      return FPK_ERR_CUDA;
+    opted[dev].store(1, std::memory_order_release);
+  }
+  k<<<grid, block, smem, s>>>(p);
+  return cudaGetLastError() == cudaSuccess ? FPK_OK : FPK_ERR_CUDA;
+}
+
+template <int DT, int NF, int NC>
+static int launch_tiled_nv(const TParams& p, int nv, int grid, int block, int smem, cudaStream_t s) {
+  switch (nv) {
+    case 1: return launch_tiled_v<DT, NF, NC, 1>(p, grid, block, smem, s);
+    case 2: return launch_tiled_v<DT, NF, NC, 2>(p, grid, block, smem, s);
+    default: return launch_tiled_v<DT, NF, NC, 4>(p, grid, block, smem, s);
+  }
+}
+
+template <int DT>
+static int launch_tiled_dt(const TParams& p, int nf, int nc, int nv, int grid, int block, int smem,
+                           cudaStream_t s) {
+  switch (nf * 10 + nc) {
+    case 10: return launch_tiled_nv<DT, 1, 0>(p, nv, grid, block, smem, s);
+    case 11: return launch_tiled_nv<DT, 1, 1>(p, nv, grid, block, smem, s);
+    case 12: return launch_tiled_nv<DT, 1, 2>(p, nv, grid, block, smem, s);
+    case 20: return launch_tiled_nv<DT, 2, 0>(p, nv, grid, block, smem, s);
+    case 21: return launch_tiled_nv<DT, 2, 1>(p, nv, grid, block, smem, s);
+    case 30: return launch_tiled_nv<DT, 3, 0>(p, nv, grid, block, smem, s);
+    default: return FPK_ERR_UNSUPPORTED;
+  }
+}
+
+// Row-tiled flat chain for the common operand shapes; FPK_ERR_UNSUPPORTED means
+// "use the general flat kernel", any other code is final.
+static int try_launch_tiled(const fpk_chain_desc* d, const void* const* inputs, void* out, cudaStream_t stream,
+                            const DeviceInfo& dev) {
+  const int64_t C = d->cols, Rr = d->rows;
+  if (d->mode != FPK_CHAIN_FLAT || (d->flags & FPK_FLAG_NO_STAGING) || C % 8 != 0 ||
+      C > 8LL * 4 * kTConsumers)
+    return FPK_ERR_UNSUPPORTED;
+  const int dt = d->out_dtype;
+  const int esz = elt_size(dt);
+  if (reinterpret_cast<uintptr_t>(out) % 16) return FPK_ERR_UNSUPPORTED;
+  const int nin = d->n_inputs;
+  int order[FPK_CHAIN_MAX_INPUTS];
+  int nf = 0, nc = 0;
+  for (int i = 0; i < nin; ++i) {
+    const int bc = d->in_bcast[i];
+    if (d->in_dtype[i] != dt || (bc != FPK_BCAST_FULL && bc != FPK_BCAST_COL)) return FPK_ERR_UNSUPPORTED;
+    if (bc == FPK_BCAST_FULL) {
+      if (reinterpret_cast<uintptr_t>(inputs[i]) % 16) return FPK_ERR_UNSUPPORTED;
+      order[nf++] = i;
+    }
+  }
+  for (int i = 0; i < nin; ++i)
+    if (d->in_bcast[i] == FPK_BCAST_COL) order[nf + nc++] = i;
+  if (nf < 1 || nf > 3 || nc > 2 || nf + nc > 3) return FPK_ERR_UNSUPPORTED;
+  if (nc * C * 4 > kTColBudget) return FPK_ERR_UNSUPPORTED;  // exact size check below
+  // renumber the input slots into the canonical order
+  fpk_chain_desc d2 = *d;
+  int newidx[FPK_CHAIN_MAX_INPUTS];
+  for (int k = 0; k < nin; ++k) {
+    newidx[order[k]] = k;
+    d2.in_dtype[k] = d->in_dtype[order[k]];
+    d2.in_bcast[k] = d->in_bcast[order[k]];
+  }
+  for (int k = 0; k < d->n_ops; ++k) {
+    if (d2.ops[k].src_a < nin) d2.ops[k].src_a = newidx[d2.ops[k].src_a];
+    if ((d2.ops[k].opcode == FPK_OP_ADD || d2.ops[k].opcode == FPK_OP_MUL) && d2.ops[k].src_b < nin)
+      d2.ops[k].src_b = newidx[d2.ops[k].src_b];
+  }
+  if (d2.result < nin) d2.result = newidx[d2.result];
+  Compiled prog;
+  int rc = compile_program(&d2, &prog);
+  if (rc != FPK_OK) return rc;
+  if (prog.uses_tmp || prog.n < 1 || prog.n > kTMaxCode || prog.code[0] >= C_MOV_T) return FPK_ERR_UNSUPPORTED;
+  for (int pc = 1; pc < prog.n; ++pc)
+    if (prog.code[pc] < C_ADD_IN) return FPK_ERR_UNSUPPORTED;  // a later move needs the general kernel
+
+  TParams p;
+  std::memset(&p, 0, sizeof(p));
+  const int cv = static_cast<int>(C / 8);
+  int nv, teff, rps;
+  if (cv <= kTConsumers) {
+    nv = 1;
+    rps = kTConsumers / cv;
+    teff = rps * cv;
+  } else {
+    const int ncv = (cv + kTConsumers - 1) / kTConsumers;
+    nv = ncv <= 2 ? ncv : 4;
+    teff = (cv + nv - 1) / nv;
+    rps = 1;
+  }
+  const int64_t rows_per_dispatch = (4 / nv) * rps;
+  const int64_t row_bytes_all = C * esz * nf;
+  int64_t u = 24576 / (rows_per_dispatch * row_bytes_all);
+  if (u < 1) u = 1;
+  const int64_t stage_rows = rows_per_dispatch * u;
+  const int64_t stage_bytes = stage_rows * row_bytes_all;
+  if (stage_bytes > kTStageBudget / 2) return FPK_ERR_UNSUPPORTED;
+  for (int k = 0; k < nin; ++k) p.in_ptr[k] = inputs[order[k]];
+  p.out = out;
+  p.status = dev.status;
+  p.rows = Rr;
+  p.cols = C;
+  p.cv = cv;
+  p.teff = teff;
+  p.rps = rps;
+  p.stage_rows = static_cast<int32_t>(stage_rows);
+  p.dispatches = static_cast<int32_t>(u);
+  p.num_blocks = (Rr + stage_rows - 1) / stage_rows;
+  p.in_bytes = static_cast<int32_t>(stage_rows * C * esz);
+  p.stage_bytes = static_cast<int32_t>(stage_bytes);
+  int nstage = static_cast<int>(kTStageBudget / stage_bytes);
+  p.nstage = nstage < 2 ? 2 : (nstage > kMaxStages ? kMaxStages : nstage);
+  p.n_code = prog.n;
+  p.flags = d->flags;
+  for (int pc = 0; pc < prog.n; ++pc) {
+    const uint64_t c = prog.code[pc];
+    if (pc < 8) p.code_lo |= c << (8 * pc);
+    else p.code_hi |= c << (8 * (pc - 8));
+    p.imm[pc] = prog.imm[pc];
+  }
+  const int grid = static_cast<int>(p.num_blocks < dev.num_sms ? p.num_blocks : dev.num_sms);
+  const int block = ((teff + 31) / 32) * 32 + 32;
+  // masked slots may read up to (teff * nv * 8 - cols) elements past a row: pad every area
+  const int64_t over = static_cast<int64_t>(teff) * nv * 8 - C;
+  p.col_pad = static_cast<int32_t>(C + (over > 0 ? over : 0));
+  const int64_t pad_bytes = (over > 0 ? over : 0) * esz + 16;
+  p.col_pad_bytes = static_cast<int32_t>(pad_bytes);
+  if (p.nstage * p.stage_bytes + pad_bytes + 16 + nc * p.col_pad * 4LL > kTStageBudget + kTColBudget)
+    return FPK_ERR_UNSUPPORTED;
+  const int smem = static_cast<int>(((p.nstage * p.stage_bytes + pad_bytes + 15) & ~15LL) + nc * p.col_pad * 4LL);
+  return dt == FPK_F16 ? launch_tiled_dt<FPK_F16>(p, nf, nc, nv, grid, block, smem, stream)
+                       : launch_tiled_dt<FPK_F32>(p, nf, nc, nv, grid, block, smem, stream);
+}
+
 }  // namespace chain
 
 int launch_chain(const fpk_chain_desc* d, const void* const* inputs, void* out, cudaStream_t stream,
@@ -861,6 +1351,8 @@ int launch_chain(const fpk_chain_desc* d, const void* const* inputs, void* out, 
   }
 
   if (flat) {
+    rc = try_launch_tiled(d, inputs, out, stream, dev);
+    if (rc != FPK_ERR_UNSUPPORTED) return rc;
     p.num_tiles = (numel + kTile - 1) / kTile;
     p.stage_bytes = staged_bytes;
     int nstage = staged_bytes ? kStageBudget / staged_bytes : 2;
