@@ -17,6 +17,10 @@
 // order, so Q K^T of the next key tile may be issued into S_t right after the
 // P V UMMA that reads P_t from it.
 //
+// The two softmax warpgroups alternate their exponential phases (a pair of
+// turn barriers), so the tensor core works on one tile while the other tile
+// is exponentiating.
+//
 // Softmax per row (log2 domain, scale folded into one FFMA per score):
 // m = running max actually used for the exponentials; O and l are rescaled
 // only when the tile max exceeds m by more than 2^8 (P values stay <= 256 and
@@ -79,6 +83,7 @@ struct Bars {
   uint64_t q_full;
   uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
   uint64_t s_full[kTiles], p_full[kTiles], o_done[kTiles];
+  uint64_t turn[kTiles];  // ping-pong of the exponential phases of the two softmax warpgroups
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -222,6 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars.s_full[t], 1);
       mbar_init(&bars.p_full[t], kWG);
       mbar_init(&bars.o_done[t], 1);
+      mbar_init(&bars.turn[t], kWG);
     }
     mbar_init(&bars.drain, 1);
     bars.abort = 0;
@@ -416,6 +422,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+        // Ping-pong: the two warpgroups take turns at the exponentials (the MUFU
+        // bound), so each tile's P V and next Q K^T UMMAs run while the other
+        // tile is exponentiating.  Tile 0 waits for tile 1's previous turn.
+        if (ntiles == 2 && (t == 1 || j > 0)) {
+          const uint32_t par = static_cast<uint32_t>(t == 1 ? j : j - 1) & 1u;
+          if (!mbar_wait(&bars.turn[t], par, abort, p.status, limit)) {
+            ok = false;
+            break;
+          }
+        }
         const float neg_m = -m_run;
         float ls[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
         uint32_t pk[64];
@@ -431,6 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ls[(c >> 1) & 7] += p1;
           pk[c >> 1] = pack_half2(p0, p1);
         }
+        if (ntiles == 2) mbar_arrive(&bars.turn[1 - t]);
         l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
         tmem_st_x64(tS, pk);
         tmem_st_wait();

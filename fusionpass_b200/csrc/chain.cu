@@ -609,11 +609,13 @@ __global__ void __launch_bounds__(TPR > 32 ? TPR : 256) chain_rows_kernel(const 
 // thread.  add / mul / scale run as packed add.rn.f32x2 / mul.rn.f32x2 (per
 // lane identical to the scalar round-to-nearest ops).  TMA streams whole row
 // blocks: one bulk copy per full input per stage.
-constexpr int kTV = 32;               // elements per dispatch (4 vectors of 8)
+constexpr int kTS = 4;                // slots (8-element vectors) per dispatch
+constexpr int kTV = 8 * kTS;          // elements per dispatch
 constexpr int kTP = kTV / 2;          // packed f32 pairs per dispatch
 constexpr int kTConsumers = 512;      // 16 consumer warps + 1 producer warp (<= 96 registers)
 constexpr int kTThreads = kTConsumers + 32;
 constexpr int kTStageBudget = 128 * 1024;
+constexpr int kTSmemTotal = 224 * 1024;  // dynamic shared memory of one row-tiled CTA at most
 constexpr int kTColBudget = 64 * 1024;  // f32 copies of the per-column operands
 constexpr int kTMaxCode = 16;         // program held in two 64-bit registers
 
@@ -648,6 +650,18 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
 __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// Ordered variants: volatile asm keeps program order, which bounds how many
+// slots' operands are live at once (see t_op_in).
+__device__ __forceinline__ uint64_t f2_add_o(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm volatile("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul_o(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm volatile("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
@@ -691,7 +705,7 @@ __device__ __forceinline__ void t_lds8f(uint32_t addr, uint64_t* v) {
   asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(v[2]), "=l"(v[3]) : "r"(addr + 16));
 }
 
-// Addressing of the 4 slots of a dispatch: slot q is vector (q % NV) of row
+// Addressing of the kTS slots of a dispatch: slot q is vector (q % NV) of row
 // (q / NV) of the thread's row step, so every address is affine in q with
 // warp-uniform strides and only one base offset per dispatch is kept.
 template <int NF, int NC>
@@ -701,30 +715,68 @@ struct TCtx {
   uint32_t row_stride;               // bytes between the rows of consecutive slots (rps rows)
   uint32_t vec_stride;               // bytes between vectors of consecutive slots (teff vectors)
   uint32_t col_stride;               // bytes between per-column vectors of consecutive slots
+  uint32_t col_half;                 // bytes from the first to the second 4 floats of a vector
 };
 
-// acc (op) operand I (compile-time, canonical order) for the 4 slots at offset e0
-template <int DT, int NF, int NC, int NV, int I, int OP>
-__device__ __forceinline__ void t_op_in(const TCtx<NF, NC>& cx, uint32_t e0, uint64_t* acc) {
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint64_t v[4];
-    if constexpr (I < NF) {
-      t_lds8<DT>(cx.in_base[I < NF ? I : 0] + e0 + (q / NV) * cx.row_stride + (q % NV) * cx.vec_stride, v);
+// acc (op) operand I (compile-time, canonical order) for the kTS slots at offset e0.
+// Software-pipelined: the shared-memory load of slot q+1 is issued before slot
+// q is combined, and the volatile loads / packed ops keep exactly that order,
+// so only two slots' operands are live at a time (no spills at 96 registers).
+// One slot of operand I: f16 data stays as 4 packed half2 words (raw[0..3]);
+// f32 data is loaded straight into 4 packed f32 pairs (pair[0..3]).
+template <int DT, int NF, int NC, int NV, int I>
+__device__ __forceinline__ void t_load_slot(const TCtx<NF, NC>& cx, uint32_t e0, int q, uint32_t* raw,
+                                            uint64_t* pair) {
+  if constexpr (I < NF) {
+    const uint32_t a = cx.in_base[I < NF ? I : 0] + e0 + (q / NV) * cx.row_stride + (q % NV) * cx.vec_stride;
+    if constexpr (DT == FPK_F16) {
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(raw[0]), "=r"(raw[1]), "=r"(raw[2]), "=r"(raw[3]) : "r"(a));
     } else {
-      t_lds8f(cx.col[I < NF ? 0 : I - NF] + (q % NV) * cx.col_stride, v);
+      asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(pair[0]), "=l"(pair[1]) : "r"(a));
+      asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(pair[2]), "=l"(pair[3]) : "r"(a + 16));
     }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      uint64_t& a = acc[q * 4 + k];
-      if constexpr (OP == 0) a = v[k];
-      else if constexpr (OP == 1) a = f2_add(a, v[k]);
-      else a = f2_mul(a, v[k]);
-    }
+  } else {
+    const uint32_t a = cx.col[I < NF ? 0 : I - NF] + (q % NV) * cx.col_stride;
+    asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(pair[0]), "=l"(pair[1]) : "r"(a));
+    asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(pair[2]), "=l"(pair[3]) : "r"(a + cx.col_half));
   }
 }
 
-template <int DT, int NF, int NC, int NV>
+template <int DT, int NF, int OP, int I>
+__device__ __forceinline__ void t_combine_slot(const uint32_t* raw, const uint64_t* pair, uint64_t* acc4) {
+  uint64_t v[4];
+  if constexpr (I < NF && DT == FPK_F16) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = h2_to_f2(raw[k]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = pair[k];
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if constexpr (OP == 0) acc4[k] = v[k];
+    else if constexpr (OP == 1) acc4[k] = f2_add_o(acc4[k], v[k]);
+    else acc4[k] = f2_mul_o(acc4[k], v[k]);
+  }
+}
+
+template <int DT, int NF, int NC, int NV, int I, int OP>
+__device__ __forceinline__ void t_op_in(const TCtx<NF, NC>& cx, uint32_t e0, uint64_t* acc) {
+  uint32_t raw[2][4];
+  uint64_t pair[2][4];
+  t_load_slot<DT, NF, NC, NV, I>(cx, e0, 0, raw[0], pair[0]);
+#pragma unroll
+  for (int q = 0; q < kTS; ++q) {
+    if (q + 1 < kTS) t_load_slot<DT, NF, NC, NV, I>(cx, e0, q + 1, raw[(q + 1) & 1], pair[(q + 1) & 1]);
+    t_combine_slot<DT, NF, OP, I>(raw[q & 1], pair[q & 1], &acc[q * 4]);
+  }
+}
+
+// TR: the program has exp / gelu.  Their unrolled expansions over 32 live
+// elements set the register peak of the whole dispatch switch, so programs
+// without them get an instance that does not contain those cases at all.
+template <int DT, int NF, int NC, int NV, bool TR>
 __device__ __forceinline__ void run_tiled(const TParams& p, const TCtx<NF, NC>& cx, uint32_t e0, uint64_t* acc) {
   uint64_t lo = p.code_lo, hi = p.code_hi;
   // the first micro-op moves an operand into acc; every later one updates acc in place
@@ -777,17 +829,21 @@ __device__ __forceinline__ void run_tiled(const TParams& p, const TCtx<NF, NC>& 
         }
         break;
       case C_EXP:
+        if constexpr (TR) {
 #pragma unroll
-        for (int k = 0; k < kTP; ++k) {
-          const float2 f = f2_unpack(acc[k]);
-          acc[k] = f2_pack(expf(f.x), expf(f.y));
+          for (int k = 0; k < kTP; ++k) {
+            const float2 f = f2_unpack(acc[k]);
+            acc[k] = f2_pack(expf(f.x), expf(f.y));
+          }
         }
         break;
       case C_GELU:
+        if constexpr (TR) {
 #pragma unroll
-        for (int k = 0; k < kTP; ++k) {
-          const float2 f = f2_unpack(acc[k]);
-          acc[k] = f2_pack(op_gelu(f.x), op_gelu(f.y));
+          for (int k = 0; k < kTP; ++k) {
+            const float2 f = f2_unpack(acc[k]);
+            acc[k] = f2_pack(op_gelu(f.x), op_gelu(f.y));
+          }
         }
         break;
       default:
@@ -813,9 +869,9 @@ __device__ __forceinline__ void t_st8(void* base, int64_t idx, const uint64_t* v
   }
 }
 
-// NV = 8-column vectors a thread owns per row (1, 2 or 4); slot s of a dispatch
-// is vector (s % NV) of row (s / NV) of the thread's current row step.
-template <int DT, int NF, int NC, int NV>
+// NV = 8-column vectors a thread owns per row (1 or 2); slot q of a dispatch
+// is vector (q % NV) of row (q / NV) of the thread's current row step.
+template <int DT, int NF, int NC, int NV, bool TR>
 __global__ void __launch_bounds__(kTThreads, 1) chain_tiled_kernel(const __grid_constant__ TParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full_bar[kMaxStages];
@@ -827,7 +883,7 @@ __global__ void __launch_bounds__(kTThreads, 1) chain_tiled_kernel(const __grid_
   const int lane = threadIdx.x & 31;
   const int ncw = (p.teff + 31) >> 5;  // consumer warps; the producer is warp ncw
   const int nstage = p.nstage;
-  // column area after the stages and the read-overrun padding (16-byte aligned)
+  // layout: input stages | read-overrun padding | column area (16-byte aligned)
   float* cols = reinterpret_cast<float*>(
       smem + ((static_cast<size_t>(nstage) * p.stage_bytes + p.col_pad_bytes + 15) & ~static_cast<size_t>(15)));
   if (threadIdx.x == 0) {
@@ -838,12 +894,18 @@ __global__ void __launch_bounds__(kTThreads, 1) chain_tiled_kernel(const __grid_
     abort_flag = 0;
     fence_mbar_init();
   }
-  // per-column operands -> f32 in shared memory (all threads of the CTA help); the
-  // padding past cols (read by masked slots only) is zero-filled
+  // per-column operands -> f32 in shared memory (all threads of the CTA help).
+  // Vector v's first 4 floats go to half A at [4v, 4v+4), the other 4 to half B
+  // (col_pad / 2 floats later), so a warp reading one half per thread touches
+  // consecutive 16-byte chunks.  The padding past cols (read by masked slots
+  // only) is zero-filled.
 #pragma unroll
   for (int j = 0; j < NC; ++j)
-    for (int c = threadIdx.x; c < p.col_pad; c += blockDim.x)
-      cols[j * p.col_pad + c] = c < p.cols ? ld1(p.in_ptr[NF + j], c, DT) : 0.0f;
+    for (int c = threadIdx.x; c < p.col_pad; c += blockDim.x) {
+      const int v = c >> 3, k = c & 7;
+      cols[j * p.col_pad + (k < 4 ? 0 : p.col_pad / 2) + v * 4 + (k & 3)] =
+          c < p.cols ? ld1(p.in_ptr[NF + j], c, DT) : 0.0f;
+    }
   __syncthreads();
   const uint64_t limit = (p.flags & FPK_FLAG_TEST_TIMEOUT) ? kTestWaitLimitNs : kWaitLimitNs;
   const int64_t G = gridDim.x;
@@ -893,18 +955,19 @@ __global__ void __launch_bounds__(kTThreads, 1) chain_tiled_kernel(const __grid_
   const bool active = t < p.teff;
   const int my_row0 = NV == 1 ? t / p.cv : 0;
   const int my_vec0 = NV == 1 ? t % p.cv : t;
-  constexpr int kRD = 4 / NV;  // rows per dispatch of one thread
+  constexpr int kRD = kTS / NV;  // rows per dispatch of one thread
   const int rows_per_dispatch = kRD * p.rps;
   const uint32_t smem0 = smem_u32(smem);
   TCtx<NF, NC> cx;
   cx.row_stride = static_cast<uint32_t>(p.rps * C * esz);
   cx.vec_stride = static_cast<uint32_t>(p.teff * 8 * esz);
-  cx.col_stride = static_cast<uint32_t>(p.teff * 8 * 4);
+  cx.col_stride = static_cast<uint32_t>(p.teff * 4 * 4);
+  cx.col_half = static_cast<uint32_t>(p.col_pad / 2 * 4);
 #pragma unroll
-  for (int j = 0; j < NC; ++j) cx.col[j] = smem_u32(cols) + static_cast<uint32_t>((j * p.col_pad + my_vec0 * 8) * 4);
+  for (int j = 0; j < NC; ++j) cx.col[j] = smem_u32(cols) + static_cast<uint32_t>((j * p.col_pad + my_vec0 * 4) * 4);
   uint32_t vec_ok = 0;  // bit q: the vector of slot q lies inside the row
 #pragma unroll
-  for (int q = 0; q < 4; ++q) vec_ok |= (my_vec0 + (q % NV) * p.teff < p.cv ? 1u : 0u) << q;
+  for (int q = 0; q < kTS; ++q) vec_ok |= (my_vec0 + (q % NV) * p.teff < p.cv ? 1u : 0u) << q;
   const uint32_t e_thread = static_cast<uint32_t>((my_row0 * C + my_vec0 * 8) * esz);
   const uint32_t e_dispatch = static_cast<uint32_t>(rows_per_dispatch * C * esz);
   uint64_t acc[kTP];
@@ -924,10 +987,10 @@ __global__ void __launch_bounds__(kTThreads, 1) chain_tiled_kernel(const __grid_
 #pragma unroll 1
       for (int u = 0; u < p.dispatches; ++u) {
         const uint32_t e0 = e_thread + static_cast<uint32_t>(u) * e_dispatch;
-        run_tiled<DT, NF, NC, NV>(p, cx, e0, acc);
+        run_tiled<DT, NF, NC, NV, TR>(p, cx, e0, acc);
         const int row0 = u * rows_per_dispatch + my_row0;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < kTS; ++q) {
           if (((vec_ok >> q) & 1u) && row0 + (q / NV) * p.rps < nr)
             t_st8<DT>(out_blk + e0 + (q / NV) * cx.row_stride + (q % NV) * cx.vec_stride, 0, &acc[q * 4]);
         }
@@ -1135,15 +1198,14 @@ static int launch_rows_n(const Params& p, int num_sms, cudaStream_t s) {
   return launch_rows_cfg<NIN, 512, 8>(p, num_sms, s);
 }
 
-template <int DT, int NF, int NC, int NV>
+template <int DT, int NF, int NC, int NV, bool TR>
 static int launch_tiled_v(const TParams& p, int grid, int block, int smem, cudaStream_t s) {
   static std::atomic<int> opted[64];
-  auto k = chain_tiled_kernel<DT, NF, NC, NV>;
+  auto k = chain_tiled_kernel<DT, NF, NC, NV, TR>;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FPK_ERR_CUDA;
   if (!opted[dev].load(std::memory_order_acquire)) {
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kTStageBudget + kTColBudget) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemTotal) != cudaSuccess)
       return FPK_ERR_CUDA;
     opted[dev].store(1, std::memory_order_release);
   }
@@ -1152,24 +1214,24 @@ static int launch_tiled_v(const TParams& p, int grid, int block, int smem, cudaS
 }
 
 template <int DT, int NF, int NC>
-static int launch_tiled_nv(const TParams& p, int nv, int grid, int block, int smem, cudaStream_t s) {
-  switch (nv) {
-    case 1: return launch_tiled_v<DT, NF, NC, 1>(p, grid, block, smem, s);
-    case 2: return launch_tiled_v<DT, NF, NC, 2>(p, grid, block, smem, s);
-    default: return launch_tiled_v<DT, NF, NC, 4>(p, grid, block, smem, s);
-  }
+static int launch_tiled_nv(const TParams& p, int nv, bool tr, int grid, int block, int smem, cudaStream_t s) {
+  if (nv == 1)
+    return tr ? launch_tiled_v<DT, NF, NC, 1, true>(p, grid, block, smem, s)
+              : launch_tiled_v<DT, NF, NC, 1, false>(p, grid, block, smem, s);
+  return tr ? launch_tiled_v<DT, NF, NC, 2, true>(p, grid, block, smem, s)
+            : launch_tiled_v<DT, NF, NC, 2, false>(p, grid, block, smem, s);
 }
 
 template <int DT>
-static int launch_tiled_dt(const TParams& p, int nf, int nc, int nv, int grid, int block, int smem,
+static int launch_tiled_dt(const TParams& p, int nf, int nc, int nv, bool tr, int grid, int block, int smem,
                            cudaStream_t s) {
   switch (nf * 10 + nc) {
-    case 10: return launch_tiled_nv<DT, 1, 0>(p, nv, grid, block, smem, s);
-    case 11: return launch_tiled_nv<DT, 1, 1>(p, nv, grid, block, smem, s);
-    case 12: return launch_tiled_nv<DT, 1, 2>(p, nv, grid, block, smem, s);
-    case 20: return launch_tiled_nv<DT, 2, 0>(p, nv, grid, block, smem, s);
-    case 21: return launch_tiled_nv<DT, 2, 1>(p, nv, grid, block, smem, s);
-    case 30: return launch_tiled_nv<DT, 3, 0>(p, nv, grid, block, smem, s);
+    case 10: return launch_tiled_nv<DT, 1, 0>(p, nv, tr, grid, block, smem, s);
+    case 11: return launch_tiled_nv<DT, 1, 1>(p, nv, tr, grid, block, smem, s);
+    case 12: return launch_tiled_nv<DT, 1, 2>(p, nv, tr, grid, block, smem, s);
+    case 20: return launch_tiled_nv<DT, 2, 0>(p, nv, tr, grid, block, smem, s);
+    case 21: return launch_tiled_nv<DT, 2, 1>(p, nv, tr, grid, block, smem, s);
+    case 30: return launch_tiled_nv<DT, 3, 0>(p, nv, tr, grid, block, smem, s);
     default: return FPK_ERR_UNSUPPORTED;
   }
 }
@@ -1180,7 +1242,7 @@ static int try_launch_tiled(const fpk_chain_desc* d, const void* const* inputs, 
                             const DeviceInfo& dev) {
   const int64_t C = d->cols, Rr = d->rows;
   if (d->mode != FPK_CHAIN_FLAT || (d->flags & FPK_FLAG_NO_STAGING) || C % 8 != 0 ||
-      C > 8LL * 4 * kTConsumers)
+      C > 8LL * 2 * kTConsumers)  // at most 2 vectors per row per thread
     return FPK_ERR_UNSUPPORTED;
   const int dt = d->out_dtype;
   const int esz = elt_size(dt);
@@ -1230,12 +1292,11 @@ static int try_launch_tiled(const fpk_chain_desc* d, const void* const* inputs, 
     rps = kTConsumers / cv;
     teff = rps * cv;
   } else {
-    const int ncv = (cv + kTConsumers - 1) / kTConsumers;
-    nv = ncv <= 2 ? ncv : 4;
+    nv = 2;  // cv <= 2 * kTConsumers was checked above
     teff = (cv + nv - 1) / nv;
     rps = 1;
   }
-  const int64_t rows_per_dispatch = (4 / nv) * rps;
+  const int64_t rows_per_dispatch = (kTS / nv) * rps;
   const int64_t row_bytes_all = C * esz * nf;
   int64_t u = 24576 / (rows_per_dispatch * row_bytes_all);
   if (u < 1) u = 1;
@@ -1255,8 +1316,6 @@ static int try_launch_tiled(const fpk_chain_desc* d, const void* const* inputs, 
   p.num_blocks = (Rr + stage_rows - 1) / stage_rows;
   p.in_bytes = static_cast<int32_t>(stage_rows * C * esz);
   p.stage_bytes = static_cast<int32_t>(stage_bytes);
-  int nstage = static_cast<int>(kTStageBudget / stage_bytes);
-  p.nstage = nstage < 2 ? 2 : (nstage > kMaxStages ? kMaxStages : nstage);
   p.n_code = prog.n;
   p.flags = d->flags;
   for (int pc = 0; pc < prog.n; ++pc) {
@@ -1267,16 +1326,21 @@ static int try_launch_tiled(const fpk_chain_desc* d, const void* const* inputs, 
   }
   const int grid = static_cast<int>(p.num_blocks < dev.num_sms ? p.num_blocks : dev.num_sms);
   const int block = ((teff + 31) / 32) * 32 + 32;
-  // masked slots may read up to (teff * nv * 8 - cols) elements past a row: pad every area
+  // masked slots may read up to (teff * nv * 8 - cols) elements past a row: pad the input area
   const int64_t over = static_cast<int64_t>(teff) * nv * 8 - C;
   p.col_pad = static_cast<int32_t>(C + (over > 0 ? over : 0));
   const int64_t pad_bytes = (over > 0 ? over : 0) * esz + 16;
   p.col_pad_bytes = static_cast<int32_t>(pad_bytes);
-  if (p.nstage * p.stage_bytes + pad_bytes + 16 + nc * p.col_pad * 4LL > kTStageBudget + kTColBudget)
-    return FPK_ERR_UNSUPPORTED;
-  const int smem = static_cast<int>(((p.nstage * p.stage_bytes + pad_bytes + 15) & ~15LL) + nc * p.col_pad * 4LL);
-  return dt == FPK_F16 ? launch_tiled_dt<FPK_F16>(p, nf, nc, nv, grid, block, smem, stream)
-                       : launch_tiled_dt<FPK_F32>(p, nf, nc, nv, grid, block, smem, stream);
+  const int64_t fixed = nc * p.col_pad * 4LL + pad_bytes + 32;
+  int64_t nst = (kTSmemTotal - fixed) / stage_bytes;
+  if (nst > kTStageBudget / stage_bytes) nst = kTStageBudget / stage_bytes;
+  if (nst < 2) return FPK_ERR_UNSUPPORTED;
+  p.nstage = static_cast<int32_t>(nst > kMaxStages ? kMaxStages : nst);
+  const int smem = static_cast<int>(((p.nstage * stage_bytes + pad_bytes + 15) & ~15LL) + nc * p.col_pad * 4LL);
+  bool tr = false;
+  for (int pc = 0; pc < prog.n; ++pc) tr |= prog.code[pc] == C_EXP || prog.code[pc] == C_GELU;
+  return dt == FPK_F16 ? launch_tiled_dt<FPK_F16>(p, nf, nc, nv, tr, grid, block, smem, stream)
+                       : launch_tiled_dt<FPK_F32>(p, nf, nc, nv, tr, grid, block, smem, stream);
 }
 
 }  // namespace chain

@@ -97,7 +97,8 @@ def _cfg2_inputs(R, C, seed=0):
     return x, b, s
 
 
-@pytest.mark.parametrize("R,C", [(4096, 4096), (1, 8), (3, 12), (257, 4100), (7, 3)])
+@pytest.mark.parametrize("R,C", [(4096, 4096), (1, 8), (3, 12), (257, 4100), (7, 3), (33, 8192), (19, 5000),
+                                 (1000, 16), (5, 768), (64, 3072), (3, 8200)])
 @pytest.mark.parametrize("staging", [True, False])
 def test_cfg2_chain_vs_oracle_bit_exact(R, C, staging):
     x, b, s = _cfg2_inputs(R, C)
@@ -127,6 +128,25 @@ def test_chain_misaligned_and_row_broadcast_and_scalar():
     ops, res = oracle.body_to_program(3, body)
     ref = oracle.chain_flat([x.numpy(), rowv.numpy(), sc.numpy()], ops, res, (R, C), np.float32)
     _close(out, ref, "f32", "misaligned/row/scalar")
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.float32])
+@pytest.mark.parametrize("R,C", [(130, 96), (17, 4096), (9, 6000)])
+def test_tiled_chain_operand_orders_and_dtypes(dt, R, C):
+    """Column operands before full ones, a full operand used twice, f32 and f16:
+    the row-tiled kernel reorders operands internally; results must not change."""
+    g = torch.Generator().manual_seed(R + C)
+    b = torch.randn(C, generator=g).to(dt)
+    x = torch.randn(R, C, generator=g).to(dt)
+    y = torch.randn(R, C, generator=g).to(dt)
+    body = [{"op": "mul", "operands": ["a1", "a0"]}, {"op": "add", "operands": ["t0", "a2"]},
+            {"op": "scale", "operands": ["t1"], "factor": -0.75}, {"op": "add", "operands": ["t2", "a1"]},
+            {"op": "exp", "operands": ["t3"]}]
+    desc = kernels.chain_descriptor(3, body, input_bcast=["col", "full", "full"])
+    out = fpkern.chain([b.cuda(), x.cuda(), y.cuda()], desc, [R, C], dt)
+    ops, res = oracle.body_to_program(3, body)
+    ref = oracle.chain_flat([b.numpy(), x.numpy(), y.numpy()], ops, res, (R, C), x.numpy().dtype)
+    _close(out, ref, "f32" if dt == torch.float32 else "f16", f"tiled {dt} {R}x{C}")
 
 
 def test_chain_tree_needs_spill_registers():
