@@ -6,11 +6,12 @@
 // and P V run as f16 x f16 -> f32 UMMAs; the softmax is f32; P is rounded to
 // f16 for the P V product; O is rounded once at the store.
 //
-// CTA = 2 query tiles of 128 rows of one (batch, head), 320 threads:
+// CTA = 2 query tiles of 128 rows of one (batch, head), 384 threads:
 //   warps 0-3  softmax warpgroup of tile 0 (one thread per query row)
 //   warps 4-7  softmax warpgroup of tile 1
 //   warp  8    TMA producer: Q once, then K_j / V_j 128-key tiles into a ring
-//   warp  9    TMEM allocator + single-thread UMMA issuer
+//   warp  9    TMEM allocator + UMMA issuer (converged warp, one elected lane issues)
+//   warps 10-11 idle (they complete the third warpgroup for setmaxnreg)
 // TMEM (512 columns x 128 lanes): S_t at columns 128*t, O_t at 256 + 128*t.
 // P_t (f16, two per column) overwrites the first 64 columns of S_t and feeds
 // the P V UMMA straight from TMEM.  UMMAs issued by one thread execute in
@@ -50,9 +51,16 @@ constexpr int kTiles = 2; // query tiles per CTA
 constexpr int kWG = 128;  // softmax threads per tile
 constexpr int kTmaWarp = 8;
 constexpr int kMmaWarp = 9;
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;  // 3 warpgroups: softmax tile 0, softmax tile 1, TMA + UMMA + 2 idle warps
+// setmaxnreg split of the 384 x 168 registers the CTA is launched with:
+// 2 x 128 x 216 (softmax) + 128 x 72 (control warpgroup) = 64512.
+constexpr int kRegsSoftmax = 216;
+constexpr int kRegsCtl = 72;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsCtl <= kThreads * 168, "setmaxnreg split exceeds the launch");
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;
+constexpr uint32_t kPolyPairs = 0x52u;  // pairs (c/2) mod 8 in {1, 4, 6} use the FMA-pipe exp2
+constexpr int kTurnAt = 96;             // score column after which the exponential turn passes
 constexpr int kMinSmem = 116 * 1024;  // keeps one CTA per SM (it owns all 512 TMEM columns)
 
 template <int D>
@@ -82,8 +90,10 @@ struct Params {
 struct Bars {
   uint64_t q_full;
   uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
+  // p_full / s_free / turn: one arrival per softmax warp (lane 0 after __syncwarp)
   uint64_t s_full[kTiles], p_full[kTiles], o_done[kTiles];
-  uint64_t turn[kTiles];  // ping-pong of the exponential phases of the two softmax warpgroups
+  uint64_t s_free[kTiles];  // split layout: S_t has been read into registers
+  uint64_t turn[kTiles];    // ping-pong of the exponential phases of the two tiles
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -127,6 +137,45 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// Issue forms for the converged UMMA warp: every lane executes them and the
+// lane holding `leader` (from elect_one) issues.  A converged warp issues UMMAs
+// markedly faster than a lone lane inside a divergent branch.
+__device__ __forceinline__ uint32_t elect_one() {
+  uint32_t e;
+  asm volatile("{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\tselp.u32 %0, 1, 0, e;\n\t}" : "=r"(e));
+  return e;
+}
+__device__ __forceinline__ void mma_ss_l(uint32_t leader, uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 e, %5, 0;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(leader));
+}
+__device__ __forceinline__ void mma_ts_l(uint32_t leader, uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                         uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 e, %5, 0;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc), "r"(leader));
+}
+__device__ __forceinline__ void mma_commit_l(uint32_t leader, uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\tsetp.ne.b32 e, %1, 0;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar)),
+      "r"(leader)
+      : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -160,6 +209,114 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// three-input max / min (one instruction folds two new scores into a running value)
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float y;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+  return y;
+}
+__device__ __forceinline__ float min3(float a, float b, float c) {
+  float y;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+  return y;
+}
+
+// packed pair arithmetic on two f32 lanes (same IEEE result per lane as the scalar op)
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %4};\n\tmov.b64 z, {%5, %5};\n\t"
+      "fma.rn.f32x2 x, x, y, z;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+// d = a * b + c per lane, c broadcast
+__device__ __forceinline__ void fma2v(float& d0, float& d1, float a0, float a1, float b0, float b1, float c) {
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\tmov.b64 z, {%6, %6};\n\t"
+      "fma.rn.f32x2 x, x, y, z;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c));
+}
+__device__ __forceinline__ void sub2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "sub.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// 2^x for a pair on the FMA pipe, to offload the MUFU (16 ex2 per clock per SM).
+// Range reduction in base 2: n = rint(x) by the 1.5 * 2^23 shifter (whose low
+// mantissa bits then hold n), f = x - n in [-1/2, 1/2]; 2^f by a degree-3
+// polynomial fitted here by linear programming for minimax relative error on
+// [-1/2, 1/2] (max 7.5e-5 in f32 Horner evaluation, below the 4.9e-4 f16
+// rounding that P gets next); the result exponent is raised by n with one
+// integer add.  x is clamped at -126 first (p(f) may lie below 1, so n >= -126
+// keeps the exponent field from wrapping into the sign bit); x = -inf (masked
+// keys) then gives a value below 1.2e-38, which is 0 once P is rounded to f16.
+constexpr float kExp2C0 = 0.9999280571937561f;
+constexpr float kExp2C1 = 0.6932609677314758f;
+constexpr float kExp2C2 = 0.2426111251115799f;
+constexpr float kExp2C3 = 0.0551716685295105f;
+__device__ __forceinline__ void ex2_poly2(float& r0, float& r1, float x0, float x1) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  x0 = fmaxf(x0, -126.0f);
+  x1 = fmaxf(x1, -126.0f);
+  float t0, t1, n0, n1, f0, f1, p0, p1;
+  fma2(t0, t1, x0, x1, 1.0f, kShift);
+  sub2(n0, n1, t0, t1, kShift, kShift);
+  sub2(f0, f1, x0, x1, n0, n1);
+  fma2v(p0, p1, f0, f1, kExp2C3, kExp2C3, kExp2C2);
+  fma2v(p0, p1, p0, p1, f0, f1, kExp2C1);
+  fma2v(p0, p1, p0, p1, f0, f1, kExp2C0);
+  r0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  r1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
+__device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %3};\n\t"
+      "add.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+}
+
+// non-blocking probe of an mbarrier phase (the UMMA issuer polls two tiles)
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Warp-uniform barrier probes for the converged UMMA warp: lane 0's answer is
+// broadcast so every lane takes the same branch.
+__device__ __forceinline__ bool mbar_test_w(uint64_t* bar, uint32_t parity) {
+  return __shfl_sync(0xffffffffu, mbar_test(bar, parity) ? 1 : 0, 0) != 0;
+}
+__device__ __forceinline__ bool mbar_wait_w(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
+                                            uint64_t limit_ns) {
+  if (mbar_test_w(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (__shfl_sync(0xffffffffu, mbar_try_wait(bar, parity) ? 1 : 0, 0)) return true;
+    if ((i & 63u) == 0u) {
+      int stop = 0;
+      if ((threadIdx.x & 31) == 0) {
+        if (*abort) {
+          stop = 1;
+        } else if (globaltimer_ns() - t0 > limit_ns) {
+          record_status(status, FPK_ERR_TIMEOUT);
+          *abort = 1;
+          stop = 1;
+        }
+      }
+      if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+    }
+  }
+}
+
 // Bounded wait that ignores the abort flag: used to drain in-flight async work.
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* status) {
   const uint64_t t0 = globaltimer_ns();
@@ -168,6 +325,23 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* 
       record_status(status, FPK_ERR_TIMEOUT);
       return;
     }
+  }
+}
+
+// drain_wait for the converged UMMA warp (lane 0 decides, all lanes follow)
+__device__ __forceinline__ void drain_wait_w(uint64_t* bar, uint32_t parity, int* status) {
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    int state = 0;
+    if ((threadIdx.x & 31) == 0) {
+      if (mbar_try_wait(bar, parity)) {
+        state = 1;
+      } else if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        record_status(status, FPK_ERR_TIMEOUT);
+        state = 2;
+      }
+    }
+    if (__shfl_sync(0xffffffffu, state, 0)) return;
   }
 }
 
@@ -194,6 +368,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ Params p) {
   using C = Cfg<D>;
   constexpr int NS = C::kStages;
+  // TMEM columns: S_t at 128 t; split layout (D <= 64): O_t at 256 + 64 t and P_t at
+  // 384 + 64 t; aliased layout (D = 128): O_t at 256 + 128 t, P_t inside S_t.
+  constexpr bool kSplit = D <= 64;
+  constexpr uint32_t kOCol0 = 256u, kOStride = kSplit ? 64u : 128u;
+  constexpr uint32_t kPCol0 = kSplit ? 384u : 0u, kPStride = kSplit ? 64u : 128u;
   extern __shared__ uint8_t smem_raw[];
   __shared__ Bars bars;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -225,9 +404,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < kTiles; ++t) {
       mbar_init(&bars.s_full[t], 1);
-      mbar_init(&bars.p_full[t], kWG);
+      mbar_init(&bars.p_full[t], kWG / 32);
       mbar_init(&bars.o_done[t], 1);
-      mbar_init(&bars.turn[t], kWG);
+      mbar_init(&bars.s_free[t], kWG / 32);
+      mbar_init(&bars.turn[t], kWG / 32);
     }
     mbar_init(&bars.drain, 1);
     bars.abort = 0;
@@ -244,120 +424,185 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tbase = bars.tmem_base;
 
-  if (warp == kTmaWarp) {
-    // --------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      bool q_issued = false;
-      int last_k[NS], last_v[NS];
-      for (int s = 0; s < NS; ++s) last_k[s] = last_v[s] = -1;
-      if (!test_timeout) {  // the timeout test withholds Q on purpose
-        mbar_arrive_expect_tx(&bars.q_full, static_cast<uint32_t>(ntiles * C::kTileBytes));
-        for (int t = 0; t < ntiles; ++t)
+  if (warp >= 2 * kWG / 32) {
+    // TMA producer, UMMA issuer and two idle warps give registers to the softmax
+    setmaxnreg_dec<kRegsCtl>();
+    if (warp == kTmaWarp) {
+      // --------------------------------------------------------- TMA producer
+      if (lane == 0) {
+        bool q_issued = false;
+        int last_k[NS], last_v[NS];
+        for (int s = 0; s < NS; ++s) last_k[s] = last_v[s] = -1;
+        if (!test_timeout) {  // the timeout test withholds Q on purpose
+          mbar_arrive_expect_tx(&bars.q_full, static_cast<uint32_t>(ntiles * C::kTileBytes));
+          for (int t = 0; t < ntiles; ++t)
+            for (int bx = 0; bx < C::kBoxes; ++bx)
+              tma_load_4d(sQ + t * C::kTileBytes + bx * C::kBoxBytes, &tq, bx * C::kBoxCols, m0 + t * kBM, hh,
+                          bb, &bars.q_full);
+          q_issued = true;
+        }
+        for (int j = 0; j < nkv; ++j) {
+          const int s = j % NS;
+          const uint32_t r = static_cast<uint32_t>(j / NS);
+          if (!mbar_wait(&bars.k_empty[s], (r & 1u) ^ 1u, abort, p.status, limit)) break;
+          mbar_arrive_expect_tx(&bars.k_full[s], C::kTileBytes);
           for (int bx = 0; bx < C::kBoxes; ++bx)
-            tma_load_4d(sQ + t * C::kTileBytes + bx * C::kBoxBytes, &tq, bx * C::kBoxCols, m0 + t * kBM, hh,
-                        bb, &bars.q_full);
-        q_issued = true;
+            tma_load_4d(sK + s * C::kTileBytes + bx * C::kBoxBytes, &tk, bx * C::kBoxCols, j * kBN, hh, bb,
+                        &bars.k_full[s]);
+          last_k[s] = j;
+          if (!mbar_wait(&bars.v_empty[s], (r & 1u) ^ 1u, abort, p.status, limit)) break;
+          mbar_arrive_expect_tx(&bars.v_full[s], C::kTileBytes);
+          for (int bx = 0; bx < C::kBoxes; ++bx)
+            tma_load_4d(sV + s * C::kTileBytes + bx * C::kBoxBytes, &tv, bx * C::kBoxCols, j * kBN, hh, bb,
+                        &bars.v_full[s]);
+          last_v[s] = j;
+        }
+        // no TMA write may land after the CTA has gone
+        if (q_issued) drain_wait(&bars.q_full, 0, p.status);
+        for (int s = 0; s < NS; ++s) {
+          if (last_k[s] >= 0) drain_wait(&bars.k_full[s], static_cast<uint32_t>(last_k[s] / NS) & 1u, p.status);
+          if (last_v[s] >= 0) drain_wait(&bars.v_full[s], static_cast<uint32_t>(last_v[s] / NS) & 1u, p.status);
+        }
       }
-      for (int j = 0; j < nkv; ++j) {
-        const int s = j % NS;
-        const uint32_t r = static_cast<uint32_t>(j / NS);
-        if (!mbar_wait(&bars.k_empty[s], (r & 1u) ^ 1u, abort, p.status, limit)) break;
-        mbar_arrive_expect_tx(&bars.k_full[s], C::kTileBytes);
-        for (int bx = 0; bx < C::kBoxes; ++bx)
-          tma_load_4d(sK + s * C::kTileBytes + bx * C::kBoxBytes, &tk, bx * C::kBoxCols, j * kBN, hh, bb,
-                      &bars.k_full[s]);
-        last_k[s] = j;
-        if (!mbar_wait(&bars.v_empty[s], (r & 1u) ^ 1u, abort, p.status, limit)) break;
-        mbar_arrive_expect_tx(&bars.v_full[s], C::kTileBytes);
-        for (int bx = 0; bx < C::kBoxes; ++bx)
-          tma_load_4d(sV + s * C::kTileBytes + bx * C::kBoxBytes, &tv, bx * C::kBoxCols, j * kBN, hh, bb,
-                      &bars.v_full[s]);
-        last_v[s] = j;
-      }
-      // no TMA write may land after the CTA has gone
-      if (q_issued) drain_wait(&bars.q_full, 0, p.status);
-      for (int s = 0; s < NS; ++s) {
-        if (last_k[s] >= 0) drain_wait(&bars.k_full[s], static_cast<uint32_t>(last_k[s] / NS) & 1u, p.status);
-        if (last_v[s] >= 0) drain_wait(&bars.v_full[s], static_cast<uint32_t>(last_v[s] / NS) & 1u, p.status);
-      }
-    }
-  } else if (warp == kMmaWarp) {
-    // ----------------------------------------------------------- UMMA issuer
-    if (lane == 0) {
+    } else if (warp == kMmaWarp) {
+      // ------------------------------------------------ UMMA issuer (whole warp)
+      // The warp runs converged; one elected lane issues.  Descriptors are kept
+      // as bases plus compile-time k-step offsets, ring positions as counters, so
+      // the issue path is a few instructions per UMMA.
       constexpr uint32_t idesc_qk = idesc_f16(kBM, kBN, false);
       constexpr uint32_t idesc_pv = idesc_f16(kBM, D, true);
-      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      constexpr uint64_t kTileStep = static_cast<uint64_t>(C::kTileBytes >> 4);  // descriptor units
+      const uint32_t leader = elect_one();
+      const uint64_t q_desc = sdesc(smem_u32(sQ), 16, 8 * C::kRowBytes, C::kLayout);
+      const uint64_t k_desc = sdesc(smem_u32(sK), 16, 8 * C::kRowBytes, C::kLayout);
+      const uint64_t v_desc = sdesc(smem_u32(sV), C::kBoxBytes, 8 * C::kRowBytes, C::kLayout);
       auto issue_qk = [&](int t, int s) {
         const uint32_t d_tmem = tbase + static_cast<uint32_t>(t * 128);
-#pragma unroll
+        const uint64_t a0 = q_desc + static_cast<uint64_t>(t) * kTileStep;
+        const uint64_t b0 = k_desc + static_cast<uint64_t>(s) * kTileStep;
+  #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk / C::kKStepsPerBox) * C::kBoxBytes + (kk % C::kKStepsPerBox) * 32;
-          const uint64_t a = sdesc(q_addr + t * C::kTileBytes + off, 16, 8 * C::kRowBytes, C::kLayout);
-          const uint64_t b = sdesc(k_addr + s * C::kTileBytes + off, 16, 8 * C::kRowBytes, C::kLayout);
-          mma_ss(d_tmem, a, b, idesc_qk, kk > 0 ? 1u : 0u);
+          constexpr int kSteps = C::kKStepsPerBox;
+          const uint64_t off = static_cast<uint64_t>((kk / kSteps) * (C::kBoxBytes >> 4) + (kk % kSteps) * 2);
+          mma_ss_l(leader, d_tmem, a0 + off, b0 + off, idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](int t, int s, bool accumulate) {
-        const uint32_t d_tmem = tbase + 256u + static_cast<uint32_t>(t * 128);
-        const uint32_t a_tmem = tbase + static_cast<uint32_t>(t * 128);
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t b = sdesc(v_addr + s * C::kTileBytes + kk * 16 * C::kRowBytes, C::kBoxBytes,
-                                   8 * C::kRowBytes, C::kLayout);
-          mma_ts(d_tmem, a_tmem + static_cast<uint32_t>(kk * 8), b, idesc_pv, (accumulate || kk > 0) ? 1u : 0u);
-        }
+        const uint32_t d_tmem = tbase + kOCol0 + static_cast<uint32_t>(t) * kOStride;
+        const uint32_t a_tmem = tbase + kPCol0 + static_cast<uint32_t>(t) * kPStride;
+        const uint64_t b0 = v_desc + static_cast<uint64_t>(s) * kTileStep;
+  #pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          mma_ts_l(leader, d_tmem, a_tmem + static_cast<uint32_t>(kk * 8),
+                   b0 + static_cast<uint64_t>(kk * C::kRowBytes), idesc_pv, (accumulate || kk > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(&bars.q_full, 0, abort, p.status, limit) &&
-                mbar_wait(&bars.k_full[0], 0, abort, p.status, limit);
+      bool ok = mbar_wait_w(&bars.q_full, 0, abort, p.status, limit) &&
+                mbar_wait_w(&bars.k_full[0], 0, abort, p.status, limit);
       if (ok) {
         tc_fence_after();
         for (int t = 0; t < ntiles; ++t) {
           issue_qk(t, 0);
-          mma_commit(&bars.s_full[t]);
+          mma_commit_l(leader, &bars.s_full[t]);
         }
-        mma_commit(&bars.k_empty[0]);
+        mma_commit_l(leader, &bars.k_empty[0]);
       }
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int s = j % NS;
-        const uint32_t r = static_cast<uint32_t>(j / NS);
-        const bool more = j + 1 < nkv;
-        const int s1 = (j + 1) % NS;
-        const uint32_t r1 = static_cast<uint32_t>((j + 1) / NS);
-        if (!mbar_wait(&bars.v_full[s], r & 1u, abort, p.status, limit)) break;
-        for (int t = 0; t < ntiles; ++t) {
-          if (!mbar_wait(&bars.p_full[t], static_cast<uint32_t>(j) & 1u, abort, p.status, limit)) {
-            ok = false;
-            break;
+      if constexpr (kSplit) {
+        // Per key tile j: QK_t(j+1) for each tile as soon as S_t(j) has been read
+        // out (s_free), then PV_t(j) as soon as P_t(j) is written (p_full).  The
+        // softmax warpgroups run in step, so this fixed order matches the order
+        // in which the barriers complete; the waits suspend in hardware and wake
+        // as soon as the phase completes.
+        int ks = 1 % NS, vs = 0;  // ring slots of K_{j+1} and V_j
+        uint32_t kph = NS == 1 ? 1u : 0u, vph = 0u;
+        for (int j = 0; ok && j < nkv; ++j) {
+          if (j + 1 < nkv) {
+            if (!mbar_wait_w(&bars.k_full[ks], kph, abort, p.status, limit)) break;
+            for (int t = 0; t < ntiles; ++t) {
+              if (!mbar_wait_w(&bars.s_free[t], static_cast<uint32_t>(j) & 1u, abort, p.status, limit)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_qk(t, ks);
+              mma_commit_l(leader, &bars.s_full[t]);
+            }
+            if (!ok) break;
+            mma_commit_l(leader, &bars.k_empty[ks]);
           }
-          tc_fence_after();
-          issue_pv(t, s, j > 0);
-          mma_commit(&bars.o_done[t]);
-          if (more) {
-            if (t == 0 && !mbar_wait(&bars.k_full[s1], r1 & 1u, abort, p.status, limit)) {
+          if (!mbar_wait_w(&bars.v_full[vs], vph, abort, p.status, limit)) break;
+          for (int t = 0; t < ntiles; ++t) {
+            if (!mbar_wait_w(&bars.p_full[t], static_cast<uint32_t>(j) & 1u, abort, p.status, limit)) {
               ok = false;
               break;
             }
-            issue_qk(t, s1);
-            mma_commit(&bars.s_full[t]);
+            tc_fence_after();
+            issue_pv(t, vs, j > 0);
+            mma_commit_l(leader, &bars.o_done[t]);
+          }
+          if (!ok) break;
+          mma_commit_l(leader, &bars.v_empty[vs]);
+          if (++ks == NS) {
+            ks = 0;
+            kph ^= 1u;
+          }
+          if (++vs == NS) {
+            vs = 0;
+            vph ^= 1u;
           }
         }
-        if (!ok) break;
-        mma_commit(&bars.v_empty[s]);
-        if (more) mma_commit(&bars.k_empty[s1]);
+      } else {
+        int s = 0, s1 = 1 % NS;
+        uint32_t r = 0u, r1 = NS == 1 ? 1u : 0u;
+        for (int j = 0; ok && j < nkv; ++j) {
+          const bool more = j + 1 < nkv;
+          if (!mbar_wait_w(&bars.v_full[s], r, abort, p.status, limit)) break;
+          for (int t = 0; t < ntiles; ++t) {
+            if (!mbar_wait_w(&bars.p_full[t], static_cast<uint32_t>(j) & 1u, abort, p.status, limit)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(t, s, j > 0);
+            mma_commit_l(leader, &bars.o_done[t]);
+            if (more) {
+              if (t == 0 && !mbar_wait_w(&bars.k_full[s1], r1, abort, p.status, limit)) {
+                ok = false;
+                break;
+              }
+              issue_qk(t, s1);
+              mma_commit_l(leader, &bars.s_full[t]);
+            }
+          }
+          if (!ok) break;
+          mma_commit_l(leader, &bars.v_empty[s]);
+          if (more) mma_commit_l(leader, &bars.k_empty[s1]);
+          s = s1;
+          r = r1;
+          if (++s1 == NS) {
+            s1 = 0;
+            r1 ^= 1u;
+          }
+        }
       }
       // every UMMA issued so far must finish before TMEM is freed
-      mma_commit(&bars.drain);
-      drain_wait(&bars.drain, 0, p.status);
+      mma_commit_l(leader, &bars.drain);
+      drain_wait_w(&bars.drain, 0, p.status);
     }
   } else {
     // ------------------------------------------------------ softmax + epilogue
+    setmaxnreg_inc<kRegsSoftmax>();
     const int t = warp >> 2;
     const int row = threadIdx.x & (kWG - 1);
     if (t < ntiles) {
       const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
       const uint32_t tS = tbase + lane_off + static_cast<uint32_t>(t * 128);
-      const uint32_t tO = tbase + lane_off + 256u + static_cast<uint32_t>(t * 128);
-      const float k2 = p.scale_log2;
+      const uint32_t tO = tbase + lane_off + kOCol0 + static_cast<uint32_t>(t) * kOStride;
+      const uint32_t tP = tbase + lane_off + kPCol0 + static_cast<uint32_t>(t) * kPStride;
+      // scale 0 runs as the smallest normal float: every finite score still maps to
+      // 2^0 = 1 in f32, and the masked (infinite) scores of a ragged tile to 0
+      const float k2 = p.scale_log2 == 0.0f ? 1.17549435e-38f : p.scale_log2;
+      const bool pos = k2 >= 0.0f;
+      const float init = pos ? -INFINITY : INFINITY;  // masked score: exp2(init * k2) = 0
       float m_run = -INFINITY;
       float l = 0.0f;
       bool ok = true;
@@ -369,38 +614,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         uint32_t sr[128];
         tmem_ld_x128(tS, sr);
+        if constexpr (kSplit) {
+          // S_t is in registers: the next Q K^T may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars.s_free[t]);
+        }
         const int valid = S - j * kBN;  // > 0; < 128 only on the last tile
-        // row max (or min for a negative scale) over 8 independent lanes of ILP
+        if (valid < kBN) {
+#pragma unroll
+          for (int c = 0; c < kBN; ++c)
+            if (c >= valid) sr[c] = __float_as_uint(init);
+        }
+        // row max (min for a negative scale), two scores per instruction, 8 chains
         float m8[8];
-        const float init = k2 >= 0.0f ? -INFINITY : INFINITY;
 #pragma unroll
         for (int i = 0; i < 8; ++i) m8[i] = init;
-        if (valid >= kBN) {
-          if (k2 >= 0.0f) {
+        if (pos) {
 #pragma unroll
-            for (int c = 0; c < kBN; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
-          } else {
-#pragma unroll
-            for (int c = 0; c < kBN; ++c) m8[c & 7] = fminf(m8[c & 7], __uint_as_float(sr[c]));
-          }
+          for (int c = 0; c < kBN; c += 2)
+            m8[(c >> 1) & 7] = max3(m8[(c >> 1) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
         } else {
-          if (k2 >= 0.0f) {
 #pragma unroll
-            for (int c = 0; c < kBN; ++c)
-              if (c < valid) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sr[c]));
-          } else {
-#pragma unroll
-            for (int c = 0; c < kBN; ++c)
-              if (c < valid) m8[c & 7] = fminf(m8[c & 7], __uint_as_float(sr[c]));
-          }
+          for (int c = 0; c < kBN; c += 2)
+            m8[(c >> 1) & 7] = min3(m8[(c >> 1) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
         }
-        float mx;
-        if (k2 >= 0.0f) {
-          mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-        } else {
-          mx = fminf(fminf(fminf(m8[0], m8[1]), fminf(m8[2], m8[3])), fminf(fminf(m8[4], m8[5]), fminf(m8[6], m8[7])));
-        }
+        float mx = pos ? max3(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]))
+                       : min3(min3(m8[0], m8[1], m8[2]), min3(m8[3], m8[4], m8[5]), fminf(m8[6], m8[7]));
         mx *= k2;  // row max of the log2-scaled scores
+        if constexpr (kSplit) {
+          // P V of the previous key tile must be done before O is rescaled or P_t reused
+          if (j > 0) {
+            if (!mbar_wait(&bars.o_done[t], static_cast<uint32_t>(j - 1) & 1u, abort, p.status, limit)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+        }
         if (j == 0) {
           m_run = mx;
         } else {
@@ -409,8 +660,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float alpha = need ? ex2(m_run - mx) : 1.0f;
             if (need) m_run = mx;
             l *= alpha;
-            // O_t already holds P_{j-1} V_{j-1}: the commit that signalled S_t
-            // covers every earlier UMMA of this CTA.
+            // O_t holds P_{j-1} V_{j-1}: in the aliased layout the commit that
+            // signalled S_t covers every earlier UMMA of this CTA.
             constexpr int kChunk = D < 32 ? D : 32;
 #pragma unroll
             for (int c0 = 0; c0 < D; c0 += kChunk) {
@@ -423,8 +674,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         // Ping-pong: the two warpgroups take turns at the exponentials (the MUFU
-        // bound), so each tile's P V and next Q K^T UMMAs run while the other
-        // tile is exponentiating.  Tile 0 waits for tile 1's previous turn.
+        // bound), so one tile's max, rescale and TMEM traffic -- and, in the
+        // aliased layout, its UMMAs -- overlap the other tile's exponentials.
+        // Tile 0 waits for tile 1's previous turn.
         if (ntiles == 2 && (t == 1 || j > 0)) {
           const uint32_t par = static_cast<uint32_t>(t == 1 ? j : j - 1) & 1u;
           if (!mbar_wait(&bars.turn[t], par, abort, p.status, limit)) {
@@ -433,26 +685,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         const float neg_m = -m_run;
-        float ls[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-        uint32_t pk[64];
+        float la[4] = {0.0f, 0.0f, 0.0f, 0.0f}, lb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        // p = 2^(s * scale * log2 e - m); P packed to f16 pairs in place (sr[c/2])
+        // 3 of every 8 pairs take the FMA-pipe exp2, the rest the MUFU; the turn
+        // passes to the other tile a quarter before the end, so its wake-up
+        // overlaps this tile's last exponentials.
 #pragma unroll
         for (int c = 0; c < kBN; c += 2) {
-          float p0 = ex2(fmaf(__uint_as_float(sr[c]), k2, neg_m));
-          float p1 = ex2(fmaf(__uint_as_float(sr[c + 1]), k2, neg_m));
-          if (valid < kBN) {
-            p0 = c < valid ? p0 : 0.0f;
-            p1 = c + 1 < valid ? p1 : 0.0f;
+          float x0, x1, p0, p1;
+          fma2(x0, x1, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]), k2, neg_m);
+          if ((kPolyPairs >> ((c >> 1) & 7)) & 1) {
+            ex2_poly2(p0, p1, x0, x1);
+          } else {
+            p0 = ex2(x0);  // masked keys: x = -inf, p = 0
+            p1 = ex2(x1);
           }
-          ls[(c >> 1) & 7] += p0;
-          ls[(c >> 1) & 7] += p1;
-          pk[c >> 1] = pack_half2(p0, p1);
+          add2(la[(c >> 1) & 3], lb[(c >> 1) & 3], p0, p1);
+          sr[c >> 1] = pack_half2(p0, p1);
+          if (c == kTurnAt && ntiles == 2) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.turn[1 - t]);
+          }
         }
-        if (ntiles == 2) mbar_arrive(&bars.turn[1 - t]);
-        l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
-        tmem_st_x64(tS, pk);
+        l += ((la[0] + lb[0]) + (la[1] + lb[1])) + ((la[2] + lb[2]) + (la[3] + lb[3]));
+        tmem_st_x64(tP, sr);
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&bars.p_full[t]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.p_full[t]);
       }
       // epilogue: O / l -> f16 -> swizzled staging (the Q_t buffer) -> TMA store
       if (ok && mbar_wait(&bars.o_done[t], static_cast<uint32_t>(nkv - 1) & 1u, abort, p.status, limit)) {
