@@ -171,27 +171,55 @@ def cpu_attention_rate(seconds: float, threads: int):
 
 
 # -------------------------------------------------------------- our arm
+# ------------------------------------------------------------ rank group
+class RankGroup:
+    """One process per GPU.  Barrier, max over ranks and a joint pass/fail vote for
+    the timed regions (NCCL between GPUs; the same code runs on gloo in CPU tests).
+    Every rank calls the same methods in the same order."""
+
+    def __init__(self, rank: int, world: int, device: torch.device):
+        self.rank, self.world, self.device = rank, world, device
+        self.dist = world > 1
+
+    def barrier(self) -> None:
+        if self.dist:
+            import torch.distributed as tdist
+            tdist.barrier()
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+
+    def max(self, x: float) -> float:
+        if not self.dist:
+            return float(x)
+        import torch.distributed as tdist
+        t = torch.tensor([float(x)], device=self.device, dtype=torch.float64)
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        return float(t.item())
+
+    def all_ok(self, ok: bool) -> bool:
+        """True only if every rank passed (so all ranks stop together on a failure)."""
+        if not self.dist:
+            return bool(ok)
+        import torch.distributed as tdist
+        t = torch.tensor([1 if ok else 0], device=self.device, dtype=torch.int32)
+        tdist.all_reduce(t, op=tdist.ReduceOp.MIN)
+        return bool(t.item())
+
+
+def weak_rate(world: int, steps: int, units_per_step: float, ms_max: float) -> float:
+    """Whole-job rate (units per second) when each of `world` ranks ran `steps`
+    steps of `units_per_step` on its own data and the slowest rank took `ms_max`."""
+    return world * steps * units_per_step / (ms_max * 1e-3)
+
+
 def run_ours(args, rank, world, dev):
     from fusionpass_b200 import fpkern, kernels
     from fusionpass_b200.runtime import execute_plan
 
     pk = peaks()
     traffic = ncu_traffic()
-    dist = world > 1
-    if dist:
-        import torch.distributed as tdist
-
-    def barrier():
-        if dist:
-            tdist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(ms: float) -> float:
-        if not dist:
-            return ms
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
-        return float(t.item())
+    group = RankGroup(rank, world, dev)
+    barrier, max_over_ranks = group.barrier, group.max
 
     desc = kernels.chain_descriptor(3, CFG2_BODY, input_bcast=["full", "col", "col"])
     x, b, s = chain_inputs(rank)
@@ -206,15 +234,17 @@ def run_ours(args, rank, world, dev):
     for i in range(max(args.warmup, 3)):
         step(i)
     torch.cuda.synchronize()
-    if fpkern.poll_status(dev) != 0:
-        raise RuntimeError("chain kernel reported a device-side error during warm-up")
+    if not group.all_ok(fpkern.poll_status(dev) == 0):
+        raise RuntimeError("chain kernel reported a device-side error during warm-up (on some rank)")
     # parity gate before timing: bit-exact against the oracle on this rank's data
+    same = True
     if not args.skip_check:
         from oracle import chain as oc
         ops, res = oc.body_to_program(3, CFG2_BODY)
         ref = oc.chain_flat([x.numpy(), b.numpy(), s.numpy()], ops, res, (R, C), np.float16)
-        if not np.array_equal(ys[0].cpu().numpy(), ref):
-            raise RuntimeError("chain output differs from the oracle: refusing to time it")
+        same = bool(np.array_equal(ys[0].cpu().numpy(), ref))
+    if not group.all_ok(same):
+        raise RuntimeError("chain output differs from the oracle (on some rank): refusing to time it")
 
     K = args.steps
     graph = torch.cuda.CUDAGraph()
@@ -242,7 +272,7 @@ def run_ours(args, rank, world, dev):
     clocks = clk.summary(w0 - 0.05, w1 + 0.05)
     per_launch_ms = ms / K
     chain_gbs = CHAIN_BYTES / (per_launch_ms * 1e-3) / 1e9
-    value = world * K * CHAIN_BYTES / (ms_max * 1e-3) / 1e9
+    value = weak_rate(world, K, CHAIN_BYTES, ms_max) / 1e9
 
     # ---- e2e through the public API: pinned host -> device -> execute_plan -> host
     e2e = None
@@ -276,7 +306,7 @@ def run_ours(args, rank, world, dev):
         a1.record(stream)
         barrier()
         ems = max_over_ranks(a0.elapsed_time(a1))
-        e2e = {"value": round(world * ke * CHAIN_BYTES / (ems * 1e-3) / 1e9, 2), "unit": "GB/s",
+        e2e = {"value": round(weak_rate(world, ke, CHAIN_BYTES, ems) / 1e9, 2), "unit": "GB/s",
                "h2d_bytes_per_step": int(hx.numel() * 2 + hb.numel() * 2 + hs.numel() * 2),
                "d2h_bytes_per_step": int(hy.numel() * 2), "steps": ke,
                "path": "pinned host -> device copies, execute_plan (libfpkern chain), device -> pinned host"}
@@ -289,8 +319,8 @@ def run_ours(args, rank, world, dev):
         for _ in range(3):
             fpkern.attention(q, k, v, 0.125, out=o)
         torch.cuda.synchronize()
-        if fpkern.poll_status(dev) != 0:
-            raise RuntimeError("attention kernel reported a device-side error during warm-up")
+        if not group.all_ok(fpkern.poll_status(dev) == 0):
+            raise RuntimeError("attention kernel reported a device-side error during warm-up (on some rank)")
         ka = args.attn_steps
         ag = torch.cuda.CUDAGraph()
         with torch.cuda.graph(ag, stream=torch.cuda.Stream(dev)):
@@ -308,7 +338,7 @@ def run_ours(args, rank, world, dev):
         tflops = ATT_FLOP / (ams / ka * 1e-3) / 1e12
         attention = {
             "workload": "fp_attention B8 H16 S2048 D64 f16, scale 1/8, non-causal",
-            "value": round(world * ka * ATT_FLOP / (ams_max * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "value": round(weak_rate(world, ka, ATT_FLOP, ams_max) / 1e12, 2), "unit": "TFLOP/s",
             "ms_per_step": round(ams_max / ka, 4), "steps": ka, "gpu_launches": ka,
             "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": pk["tc"], "unit": "TFLOP/s",
                          "frac": round(tflops / pk["tc"], 4),
@@ -428,14 +458,22 @@ def main(argv=None) -> int:
         import torch.distributed as tdist
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    # stdout carries exactly one JSON line: library output during the run (the NCCL
+    # version banner, for one) goes to stderr
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
     try:
         line = run_ours(args, rank, world, dev)
-        if rank == 0:
-            print(json.dumps(line), flush=True)
     finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
         if world > 1:
             import torch.distributed as tdist
             tdist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     return 0
 
 

@@ -59,7 +59,7 @@ constexpr int kRegsCtl = 72;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsCtl <= kThreads * 168, "setmaxnreg split exceeds the launch");
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;
-constexpr uint32_t kPolyPairs = 0x52u;  // pairs (c/2) mod 8 in {1, 4, 6} use the FMA-pipe exp2
+constexpr uint32_t kPolyPairs = 0x11u;  // pairs (c/2) mod 8 in {0, 4} use the FMA-pipe exp2
 constexpr int kTurnAt = 96;             // score column after which the exponential turn passes
 constexpr int kMinSmem = 116 * 1024;  // keeps one CTA per SM (it owns all 512 TMEM columns)
 
@@ -687,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float neg_m = -m_run;
         float la[4] = {0.0f, 0.0f, 0.0f, 0.0f}, lb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         // p = 2^(s * scale * log2 e - m); P packed to f16 pairs in place (sr[c/2])
-        // 3 of every 8 pairs take the FMA-pipe exp2, the rest the MUFU; the turn
+        // 2 of every 8 pairs take the FMA-pipe exp2, the rest the MUFU; the turn
         // passes to the other tile a quarter before the end, so its wake-up
         // overlaps this tile's last exponentials.
 #pragma unroll
