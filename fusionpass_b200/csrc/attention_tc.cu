@@ -9,18 +9,28 @@
 // CTA = 2 query tiles of 128 rows of one (batch, head), 384 threads:
 //   warps 0-3  softmax warpgroup of tile 0 (one thread per query row)
 //   warps 4-7  softmax warpgroup of tile 1
-//   warp  8    TMA producer: Q once, then K_j / V_j 128-key tiles into a ring
+//   warp  8    TMA producer: Q, then K_j / V_j 128-key tiles into a ring
 //   warp  9    TMEM allocator + UMMA issuer (converged warp, one elected lane issues)
 //   warps 10-11 idle (they complete the third warpgroup for setmaxnreg)
-// TMEM (512 columns x 128 lanes): S_t at columns 128*t, O_t at 256 + 128*t.
-// P_t (f16, two per column) overwrites the first 64 columns of S_t and feeds
-// the P V UMMA straight from TMEM.  UMMAs issued by one thread execute in
-// order, so Q K^T of the next key tile may be issued into S_t right after the
-// P V UMMA that reads P_t from it.
+// Two kernels share this structure:
 //
-// The two softmax warpgroups alternate their exponential phases (a pair of
-// turn barriers), so the tensor core works on one tile while the other tile
-// is exponentiating.
+// attn_tcp_kernel, D <= 64 (split TMEM layout, persistent): S_t at columns
+// 128 t, O_t at 256 + 64 t, P_t (f16, two per column) at 384 + 64 t.  Because
+// P has its own columns, Q K^T of key tile j+1 is issued as soon as the softmax
+// has read S_t(j) into registers and runs while the softmax computes P_t(j).
+// One CTA per SM walks its work items; TMEM, the K/V ring and the barrier
+// phases carry across items and O is staged in its own buffer, so an item's
+// epilogue overlaps the next item's first tiles.
+//
+// attn_tc_kernel, D = 128 (aliased TMEM layout, one CTA per work item): S_t at
+// 128 t, O_t at 256 + 128 t; P_t overwrites the first 64 columns of S_t.  UMMAs
+// issued by one thread execute in order, so Q K^T of the next key tile is
+// issued into S_t right after the P V UMMA that reads P_t from it.
+//
+// In both, the two softmax warpgroups take turns at the exponentials (a pair
+// of turn barriers, handed over before the end of each phase); 2 of every 8
+// score pairs are exponentiated on the FMA pipe (ex2_poly2) and the rest on
+// the MUFU.
 //
 // Softmax per row (log2 domain, scale folded into one FFMA per score):
 // m = running max actually used for the exponentials; O and l are rescaled
@@ -83,6 +93,7 @@ struct Params {
   int32_t heads;
   int32_t seq;
   int32_t num_mblocks;
+  int32_t num_items;  // batch * heads * num_mblocks (persistent kernel)
   float scale_log2;  // scale * log2(e)
   uint32_t flags;
 };
@@ -90,9 +101,8 @@ struct Params {
 struct Bars {
   uint64_t q_full;
   uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
-  // p_full / s_free / turn: one arrival per softmax warp (lane 0 after __syncwarp)
+  // p_full / turn: one arrival per softmax warp (lane 0 after __syncwarp)
   uint64_t s_full[kTiles], p_full[kTiles], o_done[kTiles];
-  uint64_t s_free[kTiles];  // split layout: S_t has been read into registers
   uint64_t turn[kTiles];    // ping-pong of the exponential phases of the two tiles
   uint64_t drain;
   uint32_t tmem_base;
@@ -368,11 +378,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ Params p) {
   using C = Cfg<D>;
   constexpr int NS = C::kStages;
-  // TMEM columns: S_t at 128 t; split layout (D <= 64): O_t at 256 + 64 t and P_t at
-  // 384 + 64 t; aliased layout (D = 128): O_t at 256 + 128 t, P_t inside S_t.
-  constexpr bool kSplit = D <= 64;
-  constexpr uint32_t kOCol0 = 256u, kOStride = kSplit ? 64u : 128u;
-  constexpr uint32_t kPCol0 = kSplit ? 384u : 0u, kPStride = kSplit ? 64u : 128u;
+  static_assert(D == 128, "D <= 64 runs in attn_tcp_kernel");
+  // TMEM columns: S_t at 128 t, O_t at 256 + 128 t; P_t overwrites the first 64
+  // columns of S_t (aliased layout).
+  constexpr uint32_t kOCol0 = 256u, kOStride = 128u;
+  constexpr uint32_t kPCol0 = 0u, kPStride = 128u;
   extern __shared__ uint8_t smem_raw[];
   __shared__ Bars bars;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -406,7 +416,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars.s_full[t], 1);
       mbar_init(&bars.p_full[t], kWG / 32);
       mbar_init(&bars.o_done[t], 1);
-      mbar_init(&bars.s_free[t], kWG / 32);
       mbar_init(&bars.turn[t], kWG / 32);
     }
     mbar_init(&bars.drain, 1);
@@ -506,82 +515,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit_l(leader, &bars.k_empty[0]);
       }
-      if constexpr (kSplit) {
-        // Per key tile j: QK_t(j+1) for each tile as soon as S_t(j) has been read
-        // out (s_free), then PV_t(j) as soon as P_t(j) is written (p_full).  The
-        // softmax warpgroups run in step, so this fixed order matches the order
-        // in which the barriers complete; the waits suspend in hardware and wake
-        // as soon as the phase completes.
-        int ks = 1 % NS, vs = 0;  // ring slots of K_{j+1} and V_j
-        uint32_t kph = NS == 1 ? 1u : 0u, vph = 0u;
-        for (int j = 0; ok && j < nkv; ++j) {
-          if (j + 1 < nkv) {
-            if (!mbar_wait_w(&bars.k_full[ks], kph, abort, p.status, limit)) break;
-            for (int t = 0; t < ntiles; ++t) {
-              if (!mbar_wait_w(&bars.s_free[t], static_cast<uint32_t>(j) & 1u, abort, p.status, limit)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              issue_qk(t, ks);
-              mma_commit_l(leader, &bars.s_full[t]);
-            }
-            if (!ok) break;
-            mma_commit_l(leader, &bars.k_empty[ks]);
+      int s = 0, s1 = 1 % NS;
+      uint32_t r = 0u, r1 = NS == 1 ? 1u : 0u;
+      for (int j = 0; ok && j < nkv; ++j) {
+        const bool more = j + 1 < nkv;
+        if (!mbar_wait_w(&bars.v_full[s], r, abort, p.status, limit)) break;
+        for (int t = 0; t < ntiles; ++t) {
+          if (!mbar_wait_w(&bars.p_full[t], static_cast<uint32_t>(j) & 1u, abort, p.status, limit)) {
+            ok = false;
+            break;
           }
-          if (!mbar_wait_w(&bars.v_full[vs], vph, abort, p.status, limit)) break;
-          for (int t = 0; t < ntiles; ++t) {
-            if (!mbar_wait_w(&bars.p_full[t], static_cast<uint32_t>(j) & 1u, abort, p.status, limit)) {
+          tc_fence_after();
+          issue_pv(t, s, j > 0);
+          mma_commit_l(leader, &bars.o_done[t]);
+          if (more) {
+            if (t == 0 && !mbar_wait_w(&bars.k_full[s1], r1, abort, p.status, limit)) {
               ok = false;
               break;
             }
-            tc_fence_after();
-            issue_pv(t, vs, j > 0);
-            mma_commit_l(leader, &bars.o_done[t]);
-          }
-          if (!ok) break;
-          mma_commit_l(leader, &bars.v_empty[vs]);
-          if (++ks == NS) {
-            ks = 0;
-            kph ^= 1u;
-          }
-          if (++vs == NS) {
-            vs = 0;
-            vph ^= 1u;
+            issue_qk(t, s1);
+            mma_commit_l(leader, &bars.s_full[t]);
           }
         }
-      } else {
-        int s = 0, s1 = 1 % NS;
-        uint32_t r = 0u, r1 = NS == 1 ? 1u : 0u;
-        for (int j = 0; ok && j < nkv; ++j) {
-          const bool more = j + 1 < nkv;
-          if (!mbar_wait_w(&bars.v_full[s], r, abort, p.status, limit)) break;
-          for (int t = 0; t < ntiles; ++t) {
-            if (!mbar_wait_w(&bars.p_full[t], static_cast<uint32_t>(j) & 1u, abort, p.status, limit)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_pv(t, s, j > 0);
-            mma_commit_l(leader, &bars.o_done[t]);
-            if (more) {
-              if (t == 0 && !mbar_wait_w(&bars.k_full[s1], r1, abort, p.status, limit)) {
-                ok = false;
-                break;
-              }
-              issue_qk(t, s1);
-              mma_commit_l(leader, &bars.s_full[t]);
-            }
-          }
-          if (!ok) break;
-          mma_commit_l(leader, &bars.v_empty[s]);
-          if (more) mma_commit_l(leader, &bars.k_empty[s1]);
-          s = s1;
-          r = r1;
-          if (++s1 == NS) {
-            s1 = 0;
-            r1 ^= 1u;
-          }
+        if (!ok) break;
+        mma_commit_l(leader, &bars.v_empty[s]);
+        if (more) mma_commit_l(leader, &bars.k_empty[s1]);
+        s = s1;
+        r = r1;
+        if (++s1 == NS) {
+          s1 = 0;
+          r1 ^= 1u;
         }
       }
       // every UMMA issued so far must finish before TMEM is freed
@@ -614,12 +577,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         uint32_t sr[128];
         tmem_ld_x128(tS, sr);
-        if constexpr (kSplit) {
-          // S_t is in registers: the next Q K^T may overwrite it
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bars.s_free[t]);
-        }
         const int valid = S - j * kBN;  // > 0; < 128 only on the last tile
         if (valid < kBN) {
 #pragma unroll
@@ -642,16 +599,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         float mx = pos ? max3(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]))
                        : min3(min3(m8[0], m8[1], m8[2]), min3(m8[3], m8[4], m8[5]), fminf(m8[6], m8[7]));
         mx *= k2;  // row max of the log2-scaled scores
-        if constexpr (kSplit) {
-          // P V of the previous key tile must be done before O is rescaled or P_t reused
-          if (j > 0) {
-            if (!mbar_wait(&bars.o_done[t], static_cast<uint32_t>(j - 1) & 1u, abort, p.status, limit)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-          }
-        }
         if (j == 0) {
           m_run = mx;
         } else {
@@ -660,8 +607,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float alpha = need ? ex2(m_run - mx) : 1.0f;
             if (need) m_run = mx;
             l *= alpha;
-            // O_t holds P_{j-1} V_{j-1}: in the aliased layout the commit that
-            // signalled S_t covers every earlier UMMA of this CTA.
+            // O_t holds P_{j-1} V_{j-1}: the commit that signalled S_t covers
+            // every earlier UMMA of this CTA.
             constexpr int kChunk = D < 32 ? D : 32;
 #pragma unroll
             for (int c0 = 0; c0 < D; c0 += kChunk) {
@@ -757,6 +704,436 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// ---------------------------------------------- persistent kernel, D <= 64 ---
+// One CTA per SM walks the work items (batch*head, 256-row query block)
+// blockIdx.x, blockIdx.x + gridDim.x, ...  TMEM is allocated once; the K/V ring
+// and every barrier phase run on across items; the next item's Q is loaded as
+// soon as the last Q K^T of the current item has completed, and O is staged in
+// its own buffer, so an item's epilogue overlaps the first tiles of the next.
+// Within an item the schedule is the split-layout one of attn_tc_kernel.
+struct PBars {
+  uint64_t q_full, q_empty;
+  uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
+  uint64_t s_full[kTiles], p_full[kTiles], o_done[kTiles], s_free[kTiles], turn[kTiles];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ void tma_store_4d_async(const CUtensorMap* map, const void* src, int x, int y, int z,
+                                                   int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tcp_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                    const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to,
+                    const __grid_constant__ Params p) {
+  static_assert(D <= 64, "the persistent kernel uses the split TMEM layout");
+  using C = Cfg<D>;
+  constexpr int NS = C::kStages;
+  constexpr uint32_t kOCol0 = 256u, kOStride = 64u, kPCol0 = 384u, kPStride = 64u;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ PBars bars;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kTiles * C::kTileBytes;
+  uint8_t* sV = sK + NS * C::kTileBytes;
+  uint8_t* sO = sV + NS * C::kTileBytes;  // O staging for the TMA store, one tile per softmax warpgroup
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int S = p.seq;
+  const int nkv = (S + kBN - 1) / kBN;
+  const int total = p.num_items;
+  const bool test_timeout = (p.flags & FPK_FLAG_TEST_TIMEOUT) != 0;
+  const uint64_t limit = test_timeout ? kTestWaitLimitNs : kWaitLimitNs;
+  volatile int* abort = &bars.abort;
+  auto coords = [&](int w, int& hh, int& bb, int& m0, int& ntiles) {
+    const int bh = w / p.num_mblocks;
+    m0 = (w % p.num_mblocks) * (kTiles * kBM);
+    hh = bh % p.heads;
+    bb = bh / p.heads;
+    ntiles = (m0 + kBM < S) ? 2 : 1;
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars.q_full, 1);
+    mbar_init(&bars.q_empty, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&bars.k_full[s], 1);
+      mbar_init(&bars.k_empty[s], 1);
+      mbar_init(&bars.v_full[s], 1);
+      mbar_init(&bars.v_empty[s], 1);
+    }
+    for (int t = 0; t < kTiles; ++t) {
+      mbar_init(&bars.s_full[t], 1);
+      mbar_init(&bars.p_full[t], kWG / 32);
+      mbar_init(&bars.o_done[t], 1);
+      mbar_init(&bars.s_free[t], kWG / 32);
+      mbar_init(&bars.turn[t], kWG / 32);
+    }
+    mbar_init(&bars.drain, 1);
+    bars.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&bars.tmem_base)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars.tmem_base;
+
+  if (warp >= 2 * kWG / 32) {
+    setmaxnreg_dec<kRegsCtl>();
+    if (warp == kTmaWarp) {
+      // --------------------------------------------------------- TMA producer
+      if (lane == 0) {
+        int kp = 0, vp = 0;  // ring slot of the next K / V load
+        uint32_t kph = 0u, vph = 0u;
+        int last_k[NS], last_v[NS];  // phase parity of each slot's last load, -1 if none
+        for (int s = 0; s < NS; ++s) last_k[s] = last_v[s] = -1;
+        uint32_t qn = 0;  // Q loads issued
+        bool ok = !test_timeout;  // the timeout test withholds every load on purpose
+        for (int w = blockIdx.x; ok && w < total; w += gridDim.x) {
+          int hh, bb, m0, ntiles;
+          coords(w, hh, bb, m0, ntiles);
+          // the previous item's Q tiles are free once its last Q K^T has completed
+          if (qn > 0 && !mbar_wait(&bars.q_empty, (qn - 1u) & 1u, abort, p.status, limit)) break;
+          mbar_arrive_expect_tx(&bars.q_full, static_cast<uint32_t>(ntiles * C::kTileBytes));
+          for (int t = 0; t < ntiles; ++t)
+            for (int bx = 0; bx < C::kBoxes; ++bx)
+              tma_load_4d(sQ + t * C::kTileBytes + bx * C::kBoxBytes, &tq, bx * C::kBoxCols, m0 + t * kBM, hh,
+                          bb, &bars.q_full);
+          ++qn;
+          for (int j = 0; j < nkv; ++j) {
+            if (!mbar_wait(&bars.k_empty[kp], kph ^ 1u, abort, p.status, limit)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&bars.k_full[kp], C::kTileBytes);
+            for (int bx = 0; bx < C::kBoxes; ++bx)
+              tma_load_4d(sK + kp * C::kTileBytes + bx * C::kBoxBytes, &tk, bx * C::kBoxCols, j * kBN, hh, bb,
+                          &bars.k_full[kp]);
+            last_k[kp] = static_cast<int>(kph);
+            if (++kp == NS) {
+              kp = 0;
+              kph ^= 1u;
+            }
+            if (!mbar_wait(&bars.v_empty[vp], vph ^ 1u, abort, p.status, limit)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&bars.v_full[vp], C::kTileBytes);
+            for (int bx = 0; bx < C::kBoxes; ++bx)
+              tma_load_4d(sV + vp * C::kTileBytes + bx * C::kBoxBytes, &tv, bx * C::kBoxCols, j * kBN, hh, bb,
+                          &bars.v_full[vp]);
+            last_v[vp] = static_cast<int>(vph);
+            if (++vp == NS) {
+              vp = 0;
+              vph ^= 1u;
+            }
+          }
+        }
+        // no TMA write may land after the CTA has gone
+        if (qn > 0) drain_wait(&bars.q_full, (qn - 1u) & 1u, p.status);
+        for (int s = 0; s < NS; ++s) {
+          if (last_k[s] >= 0) drain_wait(&bars.k_full[s], static_cast<uint32_t>(last_k[s]), p.status);
+          if (last_v[s] >= 0) drain_wait(&bars.v_full[s], static_cast<uint32_t>(last_v[s]), p.status);
+        }
+      }
+    } else if (warp == kMmaWarp) {
+      // ------------------------------------------------ UMMA issuer (whole warp)
+      constexpr uint32_t idesc_qk = idesc_f16(kBM, kBN, false);
+      constexpr uint32_t idesc_pv = idesc_f16(kBM, D, true);
+      constexpr uint64_t kTileStep = static_cast<uint64_t>(C::kTileBytes >> 4);
+      const uint32_t leader = elect_one();
+      const uint64_t q_desc = sdesc(smem_u32(sQ), 16, 8 * C::kRowBytes, C::kLayout);
+      const uint64_t k_desc = sdesc(smem_u32(sK), 16, 8 * C::kRowBytes, C::kLayout);
+      const uint64_t v_desc = sdesc(smem_u32(sV), C::kBoxBytes, 8 * C::kRowBytes, C::kLayout);
+      auto issue_qk = [&](int t, int s) {
+        const uint32_t d_tmem = tbase + static_cast<uint32_t>(t * 128);
+        const uint64_t a0 = q_desc + static_cast<uint64_t>(t) * kTileStep;
+        const uint64_t b0 = k_desc + static_cast<uint64_t>(s) * kTileStep;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          constexpr int kSteps = C::kKStepsPerBox;
+          const uint64_t off = static_cast<uint64_t>((kk / kSteps) * (C::kBoxBytes >> 4) + (kk % kSteps) * 2);
+          mma_ss_l(leader, d_tmem, a0 + off, b0 + off, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int t, int s, bool accumulate) {
+        const uint32_t d_tmem = tbase + kOCol0 + static_cast<uint32_t>(t) * kOStride;
+        const uint32_t a_tmem = tbase + kPCol0 + static_cast<uint32_t>(t) * kPStride;
+        const uint64_t b0 = v_desc + static_cast<uint64_t>(s) * kTileStep;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          mma_ts_l(leader, d_tmem, a_tmem + static_cast<uint32_t>(kk * 8),
+                   b0 + static_cast<uint64_t>(kk * C::kRowBytes), idesc_pv, (accumulate || kk > 0) ? 1u : 0u);
+      };
+      int kp = 0, vp = 0;  // ring slot of the next K / V to consume
+      uint32_t kph = 0u, vph = 0u;
+      uint32_t g0 = 0u, g1 = 0u;  // key iterations done by tile 0 / tile 1 (barrier phases)
+      uint32_t qn = 0u;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < total; w += gridDim.x) {
+        int hh, bb, m0, ntiles;
+        coords(w, hh, bb, m0, ntiles);
+        if (!mbar_wait_w(&bars.q_full, qn & 1u, abort, p.status, limit) ||
+            !mbar_wait_w(&bars.k_full[kp], kph, abort, p.status, limit))
+          break;
+        ++qn;
+        // S_t is free once the previous item's last S_t has been read out
+        for (int t = 0; t < ntiles; ++t) {
+          const uint32_t g = t == 0 ? g0 : g1;
+          if (g > 0u && !mbar_wait_w(&bars.s_free[t], (g - 1u) & 1u, abort, p.status, limit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_qk(t, kp);
+          mma_commit_l(leader, &bars.s_full[t]);
+        }
+        if (!ok) break;
+        mma_commit_l(leader, &bars.k_empty[kp]);
+        if (nkv == 1) mma_commit_l(leader, &bars.q_empty);
+        if (++kp == NS) {
+          kp = 0;
+          kph ^= 1u;
+        }
+        for (int j = 0; ok && j < nkv; ++j) {
+          if (j + 1 < nkv) {
+            if (!mbar_wait_w(&bars.k_full[kp], kph, abort, p.status, limit)) {
+              ok = false;
+              break;
+            }
+            for (int t = 0; t < ntiles; ++t) {
+              const uint32_t g = (t == 0 ? g0 : g1) + static_cast<uint32_t>(j);
+              if (!mbar_wait_w(&bars.s_free[t], g & 1u, abort, p.status, limit)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_qk(t, kp);
+              mma_commit_l(leader, &bars.s_full[t]);
+            }
+            if (!ok) break;
+            mma_commit_l(leader, &bars.k_empty[kp]);
+            if (j + 2 == nkv) mma_commit_l(leader, &bars.q_empty);  // the item's last Q K^T
+            if (++kp == NS) {
+              kp = 0;
+              kph ^= 1u;
+            }
+          }
+          if (!mbar_wait_w(&bars.v_full[vp], vph, abort, p.status, limit)) {
+            ok = false;
+            break;
+          }
+          for (int t = 0; t < ntiles; ++t) {
+            const uint32_t g = (t == 0 ? g0 : g1) + static_cast<uint32_t>(j);
+            if (!mbar_wait_w(&bars.p_full[t], g & 1u, abort, p.status, limit)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(t, vp, j > 0);
+            mma_commit_l(leader, &bars.o_done[t]);
+          }
+          if (!ok) break;
+          mma_commit_l(leader, &bars.v_empty[vp]);
+          if (++vp == NS) {
+            vp = 0;
+            vph ^= 1u;
+          }
+        }
+        g0 += static_cast<uint32_t>(nkv);
+        if (ntiles == 2) g1 += static_cast<uint32_t>(nkv);
+      }
+      // every UMMA issued so far must finish before TMEM is freed
+      mma_commit_l(leader, &bars.drain);
+      drain_wait_w(&bars.drain, 0, p.status);
+    }
+  } else {
+    // ------------------------------------------------------ softmax + epilogue
+    setmaxnreg_inc<kRegsSoftmax>();
+    const int t = warp >> 2;
+    const int row = threadIdx.x & (kWG - 1);
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tbase + lane_off + static_cast<uint32_t>(t * 128);
+    const uint32_t tO = tbase + lane_off + kOCol0 + static_cast<uint32_t>(t) * kOStride;
+    const uint32_t tP = tbase + lane_off + kPCol0 + static_cast<uint32_t>(t) * kPStride;
+    // scale 0 runs as the smallest normal float: every finite score still maps to
+    // 2^0 = 1 in f32, and the masked (infinite) scores of a ragged tile to 0
+    const float k2 = p.scale_log2 == 0.0f ? 1.17549435e-38f : p.scale_log2;
+    const bool pos = k2 >= 0.0f;
+    const float init = pos ? -INFINITY : INFINITY;  // masked score: exp2(init * k2) = 0
+    uint8_t* stage = sO + t * C::kTileBytes;
+    uint32_t g = 0u;   // key iterations this tile has done (barrier phases)
+    uint32_t tt = 0u;  // key iterations of two-tile items done (turn phases)
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < total; w += gridDim.x) {
+      int hh, bb, m0, ntiles;
+      coords(w, hh, bb, m0, ntiles);
+      if (t >= ntiles) continue;
+      float m_run = -INFINITY;
+      float l = 0.0f;
+      for (int j = 0; j < nkv; ++j) {
+        const uint32_t gj = g + static_cast<uint32_t>(j);
+        if (!mbar_wait(&bars.s_full[t], gj & 1u, abort, p.status, limit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sr[128];
+        tmem_ld_x128(tS, sr);
+        // S_t is in registers: the next Q K^T may overwrite it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.s_free[t]);
+        const int valid = S - j * kBN;  // > 0; < 128 only on the last tile
+        if (valid < kBN) {
+#pragma unroll
+          for (int c = 0; c < kBN; ++c)
+            if (c >= valid) sr[c] = __float_as_uint(init);
+        }
+        float m8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = init;
+        if (pos) {
+#pragma unroll
+          for (int c = 0; c < kBN; c += 2)
+            m8[(c >> 1) & 7] = max3(m8[(c >> 1) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < kBN; c += 2)
+            m8[(c >> 1) & 7] = min3(m8[(c >> 1) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        }
+        float mx = pos ? max3(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]))
+                       : min3(min3(m8[0], m8[1], m8[2]), min3(m8[3], m8[4], m8[5]), fminf(m8[6], m8[7]));
+        mx *= k2;
+        // P V of the previous key tile must be done before O is rescaled or P_t reused
+        if (j > 0) {
+          if (!mbar_wait(&bars.o_done[t], (gj - 1u) & 1u, abort, p.status, limit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        if (j == 0) {
+          m_run = mx;
+        } else {
+          const bool need = mx > m_run + kRescaleLog2;
+          if (__any_sync(0xffffffffu, need)) {
+            const float alpha = need ? ex2(m_run - mx) : 1.0f;
+            if (need) m_run = mx;
+            l *= alpha;
+            constexpr int kChunk = D < 32 ? D : 32;
+#pragma unroll
+            for (int c0 = 0; c0 < D; c0 += kChunk) {
+              uint32_t orow[kChunk];
+              tmem_ld<kChunk>(tO + static_cast<uint32_t>(c0), orow);
+#pragma unroll
+              for (int c = 0; c < kChunk; ++c) orow[c] = __float_as_uint(__uint_as_float(orow[c]) * alpha);
+              tmem_st<kChunk>(tO + static_cast<uint32_t>(c0), orow);
+            }
+          }
+        }
+        // ping-pong of the exponential phases (see attn_tc_kernel); the turn
+        // phases count only iterations in which both tiles are active
+        if (ntiles == 2 && (t == 1 || tt > 0u)) {
+          const uint32_t par = (t == 1 ? tt : tt - 1u) & 1u;
+          if (!mbar_wait(&bars.turn[t], par, abort, p.status, limit)) {
+            ok = false;
+            break;
+          }
+        }
+        const float neg_m = -m_run;
+        float la[4] = {0.0f, 0.0f, 0.0f, 0.0f}, lb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int c = 0; c < kBN; c += 2) {
+          float x0, x1, p0, p1;
+          fma2(x0, x1, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]), k2, neg_m);
+          if ((kPolyPairs >> ((c >> 1) & 7)) & 1) {
+            ex2_poly2(p0, p1, x0, x1);
+          } else {
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+          }
+          add2(la[(c >> 1) & 3], lb[(c >> 1) & 3], p0, p1);
+          sr[c >> 1] = pack_half2(p0, p1);
+          if (c == kTurnAt && ntiles == 2) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.turn[1 - t]);
+          }
+        }
+        l += ((la[0] + lb[0]) + (la[1] + lb[1])) + ((la[2] + lb[2]) + (la[3] + lb[3]));
+        tmem_st_x64(tP, sr);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.p_full[t]);
+        if (ntiles == 2) ++tt;
+      }
+      if (!ok) break;
+      g += static_cast<uint32_t>(nkv);
+      // epilogue: O / l -> f16 -> swizzled staging -> TMA store (not waited for)
+      if (!mbar_wait(&bars.o_done[t], (g - 1u) & 1u, abort, p.status, limit)) break;
+      tc_fence_after();
+      if (row == 0) bulk_wait_read_all();  // the previous store has read the staging buffer
+      named_bar_sync(1 + t, kWG);
+      constexpr int kChunk = D < 32 ? D : 32;
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += kChunk) {
+        uint32_t orow[kChunk];
+        tmem_ld<kChunk>(tO + static_cast<uint32_t>(c0), orow);
+        uint32_t h2[kChunk / 2];
+#pragma unroll
+        for (int c = 0; c < kChunk; c += 2)
+          h2[c / 2] = pack_half2(__fdiv_rn(__uint_as_float(orow[c]), l), __fdiv_rn(__uint_as_float(orow[c + 1]), l));
+#pragma unroll
+        for (int q = 0; q < kChunk / 8; ++q) {
+          const int col = c0 + q * 8;
+          const int bx = col / C::kBoxCols;
+          const uint32_t off = static_cast<uint32_t>(row * C::kRowBytes + (col % C::kBoxCols) * 2);
+          const uint32_t phys = off ^ (((off >> 7) & C::kSwzMask) << 4);
+          *reinterpret_cast<uint4*>(stage + bx * C::kBoxBytes + phys) =
+              make_uint4(h2[q * 4], h2[q * 4 + 1], h2[q * 4 + 2], h2[q * 4 + 3]);
+        }
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(1 + t, kWG);
+      if (row == 0) {
+        for (int bx = 0; bx < C::kBoxes; ++bx)
+          tma_store_4d_async(&to, stage + bx * C::kBoxBytes, bx * C::kBoxCols, m0 + t * kBM, hh, bb);
+      }
+    }
+    if (row == 0) bulk_wait_all();  // every O store has completed before the CTA exits
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kTmemCols));
+  }
+}
+
 // ------------------------------------------------------------- host side ---
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -813,6 +1190,30 @@ static int launch_d(const CUtensorMap* maps, const Params& p, int64_t blocks, cu
   return cudaGetLastError() == cudaSuccess ? FPK_OK : FPK_ERR_CUDA;
 }
 
+// persistent kernel: O staging after the Q tiles and the K / V ring
+template <int D>
+constexpr int persistent_smem() {
+  constexpr int bytes = (2 * kTiles + 2 * Cfg<D>::kStages) * Cfg<D>::kTileBytes + 1024;
+  return bytes > kMinSmem ? bytes : kMinSmem;
+}
+
+template <int D>
+static int launch_p(const CUtensorMap* maps, const Params& p, int64_t items, int num_sms, cudaStream_t s) {
+  static std::atomic<int> opted[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FPK_ERR_CUDA;
+  if (!opted[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(attn_tcp_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             persistent_smem<D>()) != cudaSuccess)
+      return FPK_ERR_CUDA;
+    opted[dev].store(1, std::memory_order_release);
+  }
+  const int64_t grid = items < num_sms ? items : num_sms;  // one CTA per SM, each walks its items
+  attn_tcp_kernel<D><<<static_cast<unsigned>(grid), kThreads, persistent_smem<D>(), s>>>(maps[0], maps[1], maps[2],
+                                                                                          maps[3], p);
+  return cudaGetLastError() == cudaSuccess ? FPK_OK : FPK_ERR_CUDA;
+}
+
 }  // namespace attn_tc
 
 int launch_attention_tc(const fpk_attn_desc* d, const void* q, const void* k, const void* v, void* o,
@@ -834,10 +1235,12 @@ int launch_attention_tc(const fpk_attn_desc* d, const void* q, const void* k, co
   p.flags = d->flags;
   const int64_t blocks = d->batch * d->heads * p.num_mblocks;
   if (blocks > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
+  p.num_items = static_cast<int32_t>(blocks);
+  const int num_sms = dev.num_sms > 0 ? dev.num_sms : 148;
   switch (d->head_dim) {
-    case 16: return launch_d<16>(maps, p, blocks, stream);
-    case 32: return launch_d<32>(maps, p, blocks, stream);
-    case 64: return launch_d<64>(maps, p, blocks, stream);
+    case 16: return launch_p<16>(maps, p, blocks, num_sms, stream);
+    case 32: return launch_p<32>(maps, p, blocks, num_sms, stream);
+    case 64: return launch_p<64>(maps, p, blocks, num_sms, stream);
     case 128: return launch_d<128>(maps, p, blocks, stream);
     default: return FPK_ERR_UNSUPPORTED;
   }
