@@ -28,6 +28,7 @@ FPK_F16 = 1
 
 FPK_FLAG_TEST_TIMEOUT = 0x1
 FPK_FLAG_NO_STAGING = 0x2
+FPK_FLAG_NO_JIT = 0x4
 
 FPK_CHAIN_MAX_INPUTS = 8
 FPK_CHAIN_MAX_OPS = 32
@@ -45,6 +46,8 @@ EXPORTS = (
     "fpk_attn_desc_init",
     "fpk_attention_fwd",
     "fpk_chain_fwd",
+    "fpk_chain_precompile",
+    "fpk_chain_jit_launches",
     "fpk_poll_status",
 )
 
@@ -139,6 +142,10 @@ def load() -> ctypes.CDLL:
         lib.fpk_chain_fwd.restype = ctypes.c_int
         lib.fpk_chain_fwd.argtypes = [ctypes.POINTER(ChainDesc), ctypes.POINTER(ctypes.c_void_p),
                                       ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+        lib.fpk_chain_precompile.restype = ctypes.c_int
+        lib.fpk_chain_precompile.argtypes = [ctypes.POINTER(ChainDesc)]
+        lib.fpk_chain_jit_launches.restype = ctypes.c_int64
+        lib.fpk_chain_jit_launches.argtypes = []
         lib.fpk_poll_status.restype = ctypes.c_int
         lib.fpk_poll_status.argtypes = [ctypes.c_int, ctypes.c_void_p]
         if lib.fpk_version() != FPK_ABI_VERSION:

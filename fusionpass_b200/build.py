@@ -24,11 +24,11 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libfpkern.so"
-SOURCES = ["fpkern.cu", "chain.cu", "attention_f32.cu", "attention_tc.cu"]
-HEADERS = ["common.cuh", "internal.h", "tmem_ops.cuh"]
+SOURCES = ["fpkern.cu", "chain.cu", "chain_jit.cu", "attention_f32.cu", "attention_tc.cu"]
+HEADERS = ["common.cuh", "internal.h", "tmem_ops.cuh", "chain_ops.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xptxas", "-v",
-                     f"-I{ROOT / 'include'}"]
+                     f"-I{ROOT / 'include'}", f"-I{BUILD}"]
 
 
 def nvcc() -> str:
@@ -60,8 +60,21 @@ def _compile(src: str, force: bool) -> tuple[str, int, str]:
     return src, p.returncode, p.stderr[-4000:]
 
 
+def _embed_ops_source() -> None:
+    """Write chain_ops.cuh as a C++ raw-string literal for the run-time compiled
+    chain kernels (chain_jit.cu), so they use the interpreter's op definitions."""
+    text = (CSRC / "chain_ops.cuh").read_text(encoding="utf-8")
+    if ')FPKOPS"' in text:
+        raise RuntimeError("chain_ops.cuh contains the raw-string delimiter")
+    inc = BUILD / "chain_ops_src.inc"
+    body = 'R"FPKOPS(' + text + ')FPKOPS"\n'
+    if not inc.exists() or inc.read_text(encoding="utf-8") != body:
+        inc.write_text(body, encoding="utf-8")
+
+
 def build(force: bool = False, verbose: bool = False) -> Path:
     BUILD.mkdir(parents=True, exist_ok=True)
+    _embed_ops_source()
     with ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
         results = list(ex.map(lambda s: _compile(s, force), SOURCES))
     for src, rc, log in results:
@@ -72,7 +85,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     objs = [BUILD / (Path(s).stem + ".o") for s in SOURCES]
     if force or _stale(LIB, objs):
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-ldl"]
         p = subprocess.run(cmd, capture_output=True, text=True)
         if p.returncode != 0:
             raise RuntimeError(f"link failed:\n{p.stderr}")

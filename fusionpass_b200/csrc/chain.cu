@@ -27,6 +27,7 @@
 #include <cmath>
 #include <cstring>
 
+#include "chain_ops.cuh"
 #include "common.cuh"
 #include "internal.h"
 
@@ -99,18 +100,7 @@ struct Params {
 };
 
 // ------------------------------------------------------- f32 element ops ---
-// max(x, 0) that propagates NaN like the reference's numpy maximum (one instruction)
-__device__ __forceinline__ float op_relu(float x) {
-  float y;
-  asm("max.NaN.f32 %0, %1, 0f00000000;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ float op_gelu(float x) {
-  const float t = __fmul_rn(x, 0.70710678118654752f);
-  const float e = erff(t);
-  return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.0f, e));
-}
+// op_relu, op_gelu: chain_ops.cuh
 
 template <int NIN, int V, int NT = kNumTmp>
 struct Regs {
@@ -1345,6 +1335,14 @@ static int try_launch_tiled(const fpk_chain_desc* d, const void* const* inputs, 
 
 }  // namespace chain
 
+int chain_precompile(const fpk_chain_desc* d) {
+  using namespace chain;
+  if (!d) return FPK_ERR_INVALID;
+  const int rc = validate(d, d->n_inputs);
+  if (rc != FPK_OK) return rc;
+  return chain_jit_precompile(d);
+}
+
 int launch_chain(const fpk_chain_desc* d, const void* const* inputs, void* out, cudaStream_t stream,
                  const DeviceInfo& dev) {
   using namespace chain;
@@ -1415,6 +1413,8 @@ int launch_chain(const fpk_chain_desc* d, const void* const* inputs, void* out, 
   }
 
   if (flat) {
+    rc = try_launch_chain_jit(d, inputs, out, stream, dev);
+    if (rc != FPK_ERR_UNSUPPORTED) return rc;
     rc = try_launch_tiled(d, inputs, out, stream, dev);
     if (rc != FPK_ERR_UNSUPPORTED) return rc;
     p.num_tiles = (numel + kTile - 1) / kTile;

@@ -1,0 +1,370 @@
+// Per-program flat chain kernels compiled at run time.
+//
+// The reference compiles one Triton kernel per fused chain: the plan emitter
+// writes fp_chain_<N> source (lib/Plan/TritonEmitter.cpp:14-65, twin
+// python/fusionpass/kernels.py:129-211) and Triton JIT-compiles it at the first
+// launch.  This is the sm_100a counterpart for flat chains: the descriptor's op
+// list becomes straight-line f32 CUDA (one SSA value per op), NVRTC compiles it
+// for sm_100a on first use, and the cubin is loaded with cudaLibraryLoadData and
+// cached by source text for the life of the process.  The interpreter kernels
+// in chain.cu stay the path for every case this tier does not take (rows mode,
+// ragged column counts, unaligned pointers, no run-time compiler, a stream
+// under capture before the first compile, the device-wait test flag).
+//
+// Generated kernel: each thread owns 8 consecutive elements of a row (one
+// 16-byte vector of f16, two of f32) per step and walks the flattened
+// [rows, cols/8] vector grid with a grid stride; column operands are reloaded
+// only when the thread's column changes, row operands when its row changes.
+// Two vectors are loaded before either is computed, for memory parallelism.
+// Full-shape operands are read and the result written with streaming
+// (evict-first) cache hints.  Arithmetic uses the same op definitions as the
+// interpreter (chain_ops.cuh, embedded below) with explicit round-to-nearest
+// adds and multiplies, so both tiers are bit-identical.
+#include <dlfcn.h>
+#include <nvrtc.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "internal.h"
+
+namespace fpk {
+namespace chain_jit {
+
+static const char kOpsSrc[] =
+#include "chain_ops_src.inc"
+    ;
+
+constexpr int kVec = 8;        // elements per thread-vector
+constexpr int kBlock = 256;    // threads per CTA of the generated kernel
+constexpr int kCtasPerSm = 8;  // 2048 resident threads per SM
+
+struct JitParams {
+  const void* in[FPK_CHAIN_MAX_INPUTS];
+  void* out;
+  long long rows, cols, ncv, nvec;
+};
+
+// ----------------------------------------------------------------- NVRTC ---
+struct Nvrtc {
+  bool ok = false;
+  decltype(&nvrtcCreateProgram) create = nullptr;
+  decltype(&nvrtcCompileProgram) compile = nullptr;
+  decltype(&nvrtcGetCUBINSize) cubin_size = nullptr;
+  decltype(&nvrtcGetCUBIN) cubin = nullptr;
+  decltype(&nvrtcGetProgramLogSize) log_size = nullptr;
+  decltype(&nvrtcGetProgramLog) log = nullptr;
+  decltype(&nvrtcDestroyProgram) destroy = nullptr;
+};
+
+static const Nvrtc& nvrtc() {
+  static Nvrtc n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* env = std::getenv("FPK_NVRTC_LIB");
+    const char* cands[] = {env, "libnvrtc.so.12", "libnvrtc.so", "/usr/local/cuda/lib64/libnvrtc.so.12"};
+    void* h = nullptr;
+    for (const char* c : cands)
+      if (c && *c && (h = dlopen(c, RTLD_NOW | RTLD_LOCAL)) != nullptr) break;
+    if (!h) return;
+    n.create = reinterpret_cast<decltype(n.create)>(dlsym(h, "nvrtcCreateProgram"));
+    n.compile = reinterpret_cast<decltype(n.compile)>(dlsym(h, "nvrtcCompileProgram"));
+    n.cubin_size = reinterpret_cast<decltype(n.cubin_size)>(dlsym(h, "nvrtcGetCUBINSize"));
+    n.cubin = reinterpret_cast<decltype(n.cubin)>(dlsym(h, "nvrtcGetCUBIN"));
+    n.log_size = reinterpret_cast<decltype(n.log_size)>(dlsym(h, "nvrtcGetProgramLogSize"));
+    n.log = reinterpret_cast<decltype(n.log)>(dlsym(h, "nvrtcGetProgramLog"));
+    n.destroy = reinterpret_cast<decltype(n.destroy)>(dlsym(h, "nvrtcDestroyProgram"));
+    n.ok = n.create && n.compile && n.cubin_size && n.cubin && n.log_size && n.log && n.destroy;
+  });
+  return n;
+}
+
+// ------------------------------------------------------- source generator ---
+// Eligibility that depends on the descriptor alone.
+static bool shape_ok(const fpk_chain_desc* d) {
+  if (d->mode != FPK_CHAIN_FLAT || d->cols <= 0 || d->rows <= 0 || d->cols % kVec) return false;
+  if (d->flags & (FPK_FLAG_TEST_TIMEOUT | FPK_FLAG_NO_STAGING | FPK_FLAG_NO_JIT)) return false;
+  for (int k = 0; k < d->n_ops; ++k) {
+    const int op = d->ops[k].opcode;
+    if (op != FPK_OP_ADD && op != FPK_OP_MUL && op != FPK_OP_SCALE && op != FPK_OP_RELU && op != FPK_OP_EXP &&
+        op != FPK_OP_GELU)
+      return false;
+  }
+  return true;
+}
+
+static void app(std::string& s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+static void app(std::string& s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  const int n = vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (n > 0) s.append(buf, static_cast<size_t>(n < static_cast<int>(sizeof(buf)) ? n : sizeof(buf) - 1));
+}
+
+static std::string gen_source(const fpk_chain_desc* d) {
+  const int nin = d->n_inputs;
+  std::string s;
+  s.reserve(8192);
+  s += "typedef unsigned int u32;\ntypedef unsigned short u16;\ntypedef long long i64;\n";
+  s += kOpsSrc;
+  s += R"SRC(
+struct JitParams { const void* in[8]; void* out; i64 rows, cols, ncv, nvec; };
+__device__ __forceinline__ float h2f(u16 h) { float f; asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h)); return f; }
+__device__ __forceinline__ u32 f2h(float f) { u16 h; asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(f)); return h; }
+__device__ __forceinline__ void unpack8(uint4 u, float* a) {
+  a[0] = h2f((u16)(u.x & 0xffffu)); a[1] = h2f((u16)(u.x >> 16));
+  a[2] = h2f((u16)(u.y & 0xffffu)); a[3] = h2f((u16)(u.y >> 16));
+  a[4] = h2f((u16)(u.z & 0xffffu)); a[5] = h2f((u16)(u.z >> 16));
+  a[6] = h2f((u16)(u.w & 0xffffu)); a[7] = h2f((u16)(u.w >> 16));
+}
+// full-shape operands: streaming loads (read once, evict first)
+__device__ __forceinline__ void ld8s_f16(const void* b, i64 off, float* a) {
+  unpack8(__ldcs(reinterpret_cast<const uint4*>(reinterpret_cast<const u16*>(b) + off)), a);
+}
+__device__ __forceinline__ void ld8s_f32(const void* b, i64 off, float* a) {
+  const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(b) + off);
+  const float4 x = __ldcs(p), y = __ldcs(p + 1);
+  a[0] = x.x; a[1] = x.y; a[2] = x.z; a[3] = x.w; a[4] = y.x; a[5] = y.y; a[6] = y.z; a[7] = y.w;
+}
+// broadcast operands: read-only cache (reused by every row)
+__device__ __forceinline__ void ld8c_f16(const void* b, i64 off, float* a) {
+  unpack8(__ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const u16*>(b) + off)), a);
+}
+__device__ __forceinline__ void ld8c_f32(const void* b, i64 off, float* a) {
+  const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(b) + off);
+  const float4 x = __ldg(p), y = __ldg(p + 1);
+  a[0] = x.x; a[1] = x.y; a[2] = x.z; a[3] = x.w; a[4] = y.x; a[5] = y.y; a[6] = y.z; a[7] = y.w;
+}
+__device__ __forceinline__ float ld1_f16(const void* b, i64 i) { return h2f(__ldg(reinterpret_cast<const u16*>(b) + i)); }
+__device__ __forceinline__ float ld1_f32(const void* b, i64 i) { return __ldg(reinterpret_cast<const float*>(b) + i); }
+__device__ __forceinline__ void st8_f16(void* b, i64 off, const float* y) {
+  uint4 u;
+  u.x = f2h(y[0]) | (f2h(y[1]) << 16); u.y = f2h(y[2]) | (f2h(y[3]) << 16);
+  u.z = f2h(y[4]) | (f2h(y[5]) << 16); u.w = f2h(y[6]) | (f2h(y[7]) << 16);
+  __stcs(reinterpret_cast<uint4*>(reinterpret_cast<u16*>(b) + off), u);
+}
+__device__ __forceinline__ void st8_f32(void* b, i64 off, const float* y) {
+  float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(b) + off);
+  __stcs(p, make_float4(y[0], y[1], y[2], y[3]));
+  __stcs(p + 1, make_float4(y[4], y[5], y[6], y[7]));
+}
+)SRC";
+  const char* dt[2] = {"f32", "f16"};
+  auto idt = [&](int i) { return dt[d->in_dtype[i] == FPK_F16 ? 1 : 0]; };
+
+  app(s, "extern \"C\" __global__ void __launch_bounds__(%d) fpk_jit_chain(const JitParams p) {\n", kBlock);
+  s += "  const i64 stride = (i64)gridDim.x * blockDim.x;\n";
+  s += "  i64 v = (i64)blockIdx.x * blockDim.x + threadIdx.x;\n";
+  s += "  if (v >= p.nvec) return;\n";
+  s += "  const i64 drow = stride / p.ncv, dcv = stride - drow * p.ncv;\n";
+  s += "  i64 row0 = v / p.ncv, cv0 = v - row0 * p.ncv;\n";
+  // broadcast operand state
+  for (int i = 0; i < nin; ++i) {
+    switch (d->in_bcast[i]) {
+      case FPK_BCAST_COL:
+        app(s, "  float c%d[8]; i64 c%d_at = -1;\n", i, i);
+        break;
+      case FPK_BCAST_ROW:
+        app(s, "  float r%d = 0.0f; i64 r%d_at = -1;\n", i, i);
+        break;
+      case FPK_BCAST_SCALAR:
+        app(s, "  const float s%d = ld1_%s(p.in[%d], 0);\n", i, idt(i), i);
+        break;
+      default:
+        break;
+    }
+  }
+  s += "  for (; v < p.nvec; v += 2 * stride) {\n";
+  s += "    const bool two = v + stride < p.nvec;\n";
+  s += "    i64 row1 = row0 + drow, cv1 = cv0 + dcv;\n";
+  s += "    if (cv1 >= p.ncv) { cv1 -= p.ncv; ++row1; }\n";
+  s += "    const i64 off0 = v * 8, off1 = (v + stride) * 8;  // element offsets (cols % 8 == 0)\n";
+  // full-shape loads for both vectors first
+  for (int i = 0; i < nin; ++i) {
+    if (d->in_bcast[i] != FPK_BCAST_FULL) continue;
+    app(s, "    float a%d_0[8], a%d_1[8];\n", i, i);
+    app(s, "    ld8s_%s(p.in[%d], off0, a%d_0);\n", idt(i), i, i);
+    app(s, "    if (two) ld8s_%s(p.in[%d], off1, a%d_1);\n", idt(i), i, i);
+  }
+  for (int u = 0; u < 2; ++u) {
+    if (u == 1) s += "    if (two) {\n";
+    const char* ind = u == 1 ? "      " : "    ";
+    app(s, "%s{\n", ind);
+    for (int i = 0; i < nin; ++i) {
+      if (d->in_bcast[i] == FPK_BCAST_COL)
+        app(s, "%s  if (cv%d != c%d_at) { ld8c_%s(p.in[%d], cv%d * 8, c%d); c%d_at = cv%d; }\n", ind, u, i, idt(i), i,
+            u, i, i, u);
+      else if (d->in_bcast[i] == FPK_BCAST_ROW)
+        app(s, "%s  if (row%d != r%d_at) { r%d = ld1_%s(p.in[%d], row%d); r%d_at = row%d; }\n", ind, u, i, i,
+            idt(i), i, u, i, u);
+    }
+    app(s, "%s  float y[8];\n", ind);
+    app(s, "%s  #pragma unroll\n", ind);
+    app(s, "%s  for (int e = 0; e < 8; ++e) {\n", ind);
+    for (int i = 0; i < nin; ++i) {
+      switch (d->in_bcast[i]) {
+        case FPK_BCAST_FULL: app(s, "%s    const float v%d = a%d_%d[e];\n", ind, i, i, u); break;
+        case FPK_BCAST_COL: app(s, "%s    const float v%d = c%d[e];\n", ind, i, i); break;
+        case FPK_BCAST_ROW: app(s, "%s    const float v%d = r%d;\n", ind, i, i); break;
+        default: app(s, "%s    const float v%d = s%d;\n", ind, i, i); break;
+      }
+    }
+    for (int k = 0; k < d->n_ops; ++k) {
+      const fpk_chain_op& op = d->ops[k];
+      const int dst = nin + k;
+      switch (op.opcode) {
+        case FPK_OP_ADD: app(s, "%s    const float v%d = __fadd_rn(v%d, v%d);\n", ind, dst, op.src_a, op.src_b); break;
+        case FPK_OP_MUL: app(s, "%s    const float v%d = __fmul_rn(v%d, v%d);\n", ind, dst, op.src_a, op.src_b); break;
+        case FPK_OP_SCALE: {
+          uint32_t bits;
+          std::memcpy(&bits, &op.imm, 4);
+          app(s, "%s    const float v%d = __fmul_rn(v%d, __uint_as_float(0x%08xu));\n", ind, dst, op.src_a, bits);
+          break;
+        }
+        case FPK_OP_RELU: app(s, "%s    const float v%d = op_relu(v%d);\n", ind, dst, op.src_a); break;
+        case FPK_OP_EXP: app(s, "%s    const float v%d = expf(v%d);\n", ind, dst, op.src_a); break;
+        default: app(s, "%s    const float v%d = op_gelu(v%d);\n", ind, dst, op.src_a); break;
+      }
+    }
+    app(s, "%s    y[e] = v%d;\n", ind, d->result);
+    app(s, "%s  }\n", ind);
+    app(s, "%s  st8_%s(p.out, off%d, y);\n", ind, d->out_dtype == FPK_F16 ? "f16" : "f32", u);
+    app(s, "%s}\n", ind);
+    if (u == 1) s += "    }\n";
+  }
+  s += "    row0 = row1 + drow; cv0 = cv1 + dcv;\n";
+  s += "    if (cv0 >= p.ncv) { cv0 -= p.ncv; ++row0; }\n";
+  s += "  }\n}\n";
+  return s;
+}
+
+// ------------------------------------------------------------------ cache ---
+struct Entry {
+  std::vector<char> cubin;
+  cudaLibrary_t lib = nullptr;
+  cudaKernel_t kern = nullptr;
+  bool failed = false;
+};
+
+static std::mutex g_mu;
+static std::atomic<long long> g_launches{0};
+static std::unordered_map<std::string, Entry>& cache() {
+  static auto* m = new std::unordered_map<std::string, Entry>();  // lives for the process
+  return *m;
+}
+
+// NVRTC compile of `src` into e.cubin (caller holds g_mu).
+static bool compile_locked(const std::string& src, Entry& e) {
+  const Nvrtc& n = nvrtc();
+  if (!n.ok) return false;
+  nvrtcProgram prog = nullptr;
+  if (n.create(&prog, src.c_str(), "fpk_jit_chain.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS) return false;
+  // same floating-point contract as the nvcc build of the interpreter
+  const char* opts[] = {"--gpu-architecture=sm_100a", "-std=c++17", "--fmad=true", "--ftz=false",
+                        "--prec-div=true", "--prec-sqrt=true", "-default-device"};
+  const nvrtcResult rc = n.compile(prog, static_cast<int>(sizeof(opts) / sizeof(opts[0])), opts);
+  bool ok = rc == NVRTC_SUCCESS;
+  if (ok) {
+    size_t sz = 0;
+    ok = n.cubin_size(prog, &sz) == NVRTC_SUCCESS && sz > 0;
+    if (ok) {
+      e.cubin.resize(sz);
+      ok = n.cubin(prog, e.cubin.data()) == NVRTC_SUCCESS;
+    }
+  } else if (std::getenv("FPK_JIT_VERBOSE")) {
+    size_t ls = 0;
+    if (n.log_size(prog, &ls) == NVRTC_SUCCESS && ls > 1) {
+      std::string log(ls, '\0');
+      n.log(prog, &log[0]);
+      std::fprintf(stderr, "[fpkern] chain JIT compile failed:\n%s\n", log.c_str());
+    }
+  }
+  n.destroy(&prog);
+  return ok;
+}
+
+}  // namespace chain_jit
+
+int chain_jit_precompile(const fpk_chain_desc* d) {
+  using namespace chain_jit;
+  if (!shape_ok(d)) return FPK_ERR_UNSUPPORTED;
+  const std::string src = gen_source(d);
+  std::lock_guard<std::mutex> lk(g_mu);
+  Entry& e = cache()[src];
+  if (e.failed) return FPK_ERR_UNSUPPORTED;
+  if (!e.cubin.empty()) return FPK_OK;
+  if (!compile_locked(src, e)) {
+    e.failed = true;
+    return FPK_ERR_UNSUPPORTED;
+  }
+  return FPK_OK;
+}
+
+int try_launch_chain_jit(const fpk_chain_desc* d, const void* const* inputs, void* out, cudaStream_t stream,
+                         const DeviceInfo& dev) {
+  using namespace chain_jit;
+  if (!shape_ok(d)) return FPK_ERR_UNSUPPORTED;
+  if (reinterpret_cast<uintptr_t>(out) % 16) return FPK_ERR_UNSUPPORTED;
+  for (int i = 0; i < d->n_inputs; ++i) {
+    const int b = d->in_bcast[i];
+    if ((b == FPK_BCAST_FULL || b == FPK_BCAST_COL) && reinterpret_cast<uintptr_t>(inputs[i]) % 16)
+      return FPK_ERR_UNSUPPORTED;
+  }
+  const std::string src = gen_source(d);
+  cudaKernel_t kern = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Entry& e = cache()[src];
+    if (e.failed) return FPK_ERR_UNSUPPORTED;
+    if (!e.kern) {
+      // compiling or loading modules is not a stream operation, but keep it out of
+      // a capture: the interpreter serves this call and the next one compiles
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+        return FPK_ERR_UNSUPPORTED;
+      if (e.cubin.empty() && !compile_locked(src, e)) {
+        e.failed = true;
+        return FPK_ERR_UNSUPPORTED;
+      }
+      if (cudaLibraryLoadData(&e.lib, e.cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0) != cudaSuccess ||
+          cudaLibraryGetKernel(&e.kern, e.lib, "fpk_jit_chain") != cudaSuccess) {
+        cudaGetLastError();
+        e.failed = true;
+        e.kern = nullptr;
+        return FPK_ERR_UNSUPPORTED;
+      }
+    }
+    kern = e.kern;
+  }
+  JitParams p;
+  std::memset(&p, 0, sizeof(p));
+  for (int i = 0; i < d->n_inputs; ++i) p.in[i] = inputs[i];
+  p.out = out;
+  p.rows = d->rows;
+  p.cols = d->cols;
+  p.ncv = d->cols / kVec;
+  p.nvec = d->rows * p.ncv;
+  const long long per_cta = static_cast<long long>(kBlock) * 2;  // two vectors per thread and step
+  long long grid = (p.nvec + per_cta - 1) / per_cta;
+  const long long cap = static_cast<long long>(dev.num_sms > 0 ? dev.num_sms : 148) * kCtasPerSm;
+  if (grid > cap) grid = cap;
+  void* args[] = {&p};
+  if (cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(static_cast<unsigned>(grid)), dim3(kBlock), args, 0,
+                       stream) != cudaSuccess)
+    return FPK_ERR_CUDA;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return FPK_OK;
+}
+
+long long chain_jit_launches() { return chain_jit::g_launches.load(std::memory_order_relaxed); }
+
+}  // namespace fpk

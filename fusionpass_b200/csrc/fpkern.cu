@@ -127,6 +127,13 @@ int fpk_chain_fwd(const fpk_chain_desc* d, const void* const* inputs, int n_inpu
   return fpk::launch_chain(d, inputs, out, static_cast<cudaStream_t>(stream), dev);
 }
 
+int fpk_chain_precompile(const fpk_chain_desc* d) {
+  if (!d || d->size != sizeof(fpk_chain_desc) || d->version != FPK_ABI_VERSION) return FPK_ERR_INVALID;
+  return fpk::chain_precompile(d);
+}
+
+int64_t fpk_chain_jit_launches(void) { return static_cast<int64_t>(fpk::chain_jit_launches()); }
+
 int fpk_poll_status(int device, void* stream) {
   int prev = -1;
   if (cudaGetDevice(&prev) != cudaSuccess) return FPK_ERR_CUDA;

@@ -153,6 +153,28 @@ def chain(inputs: Sequence[torch.Tensor], desc: Mapping[str, Any], out_shape, ou
     return out
 
 
+def precompile_chain(desc: Mapping[str, Any], cols: int, in_dtypes: Sequence[torch.dtype], bcasts: Sequence[str],
+                     out_dtype: torch.dtype, flags: int = 0) -> bool:
+    """Compile and cache the run-time specialised kernel of a flat chain before its
+    first launch (the first ``chain`` call with this op list, operand dtypes and
+    broadcast modes would do the same).  Needs no GPU.  Returns False when the
+    chain runs on the prebuilt kernels instead (rows mode, ``cols % 8 != 0``,
+    ``FPK_FLAG_NO_JIT``, or no run-time compiler in the process)."""
+    lib = _lib.load()
+    c = build_chain_desc(desc, 1, int(cols), [_TORCH_DT[dt] for dt in in_dtypes], list(bcasts),
+                         _TORCH_DT[out_dtype], flags)
+    rc = lib.fpk_chain_precompile(ctypes.byref(c))
+    if rc == _lib.FPK_ERR_UNSUPPORTED:
+        return False
+    _lib.check(rc, "fpk_chain_precompile")
+    return True
+
+
+def chain_jit_launches() -> int:
+    """Flat chains launched so far through run-time compiled kernels (diagnostic)."""
+    return int(_lib.load().fpk_chain_jit_launches())
+
+
 def _bhsd(t: torch.Tensor):
     """(B, H, S, D, strides[b, h, s]) of a [..., S, D] tensor with a unit D stride."""
     if t.dim() < 3:

@@ -1,0 +1,117 @@
+"""GPU: run-time compiled flat chains are bit-identical to the interpreter kernels
+and to the oracle, and they really run (launch counter)."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from fusionpass_b200 import _lib, fpkern, kernels
+from tests.test_chain_jit_cpu import random_chain
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean():
+    yield
+    assert fpkern.poll_status() == 0, "a kernel recorded a device-side error"
+
+
+def _bits(t):
+    """Bit pattern with every NaN mapped to one canonical value."""
+    t = t.detach()
+    if t.dtype == torch.float16:
+        return torch.where(torch.isnan(t), torch.full_like(t, float("nan")), t).view(torch.int16).cpu()
+    return torch.where(torch.isnan(t), torch.full_like(t, float("nan")), t).view(torch.int32).cpu()
+
+
+def _operand(shape_kind, R, C, dt, g):
+    n = {"full": (R, C), "col": (C,), "row": (R, 1), "scalar": (1,)}[shape_kind]
+    return (torch.randn(n, generator=g) * 2).to(dt).cuda()
+
+
+@pytest.mark.parametrize("seed", range(6))
+@pytest.mark.parametrize("R,C", [(1, 8), (37, 40), (1000, 64), (4097, 16), (2048, 4096)])
+def test_random_programs_jit_equals_interpreter(seed, R, C):
+    rng = np.random.default_rng(100 + seed)
+    g = torch.Generator().manual_seed(seed)
+    n_in = int(rng.integers(1, 5))
+    body = random_chain(rng, n_in)
+    bc = ["full"] + [["full", "col", "row", "scalar"][int(rng.integers(4))] for _ in range(n_in - 1)]
+    dts = [[torch.float16, torch.float32][int(rng.integers(2))] for _ in range(n_in)]
+    out_dt = [torch.float16, torch.float32][int(rng.integers(2))]
+    desc = kernels.chain_descriptor(n_in, body, input_bcast=bc)
+    ins = [_operand(k, R, C, dt, g) for k, dt in zip(bc, dts)]
+    n0 = fpkern.chain_jit_launches()
+    y_jit = fpkern.chain(ins, desc, [R, C], out_dt)
+    assert fpkern.chain_jit_launches() == n0 + 1, "the run-time compiled kernel did not run"
+    y_tiled = fpkern.chain(ins, desc, [R, C], out_dt, flags=_lib.FPK_FLAG_NO_JIT)
+    y_gen = fpkern.chain(ins, desc, [R, C], out_dt, flags=_lib.FPK_FLAG_NO_STAGING)
+    assert fpkern.chain_jit_launches() == n0 + 1
+    assert torch.equal(_bits(y_jit), _bits(y_tiled))
+    assert torch.equal(_bits(y_jit), _bits(y_gen))
+
+
+def test_special_values_bit_exact_vs_oracle():
+    """inf, -inf, NaN, -0.0, denormal f16 through relu / scale / add / mul."""
+    vals = torch.tensor([float("inf"), float("-inf"), float("nan"), -0.0, 0.0, 6e-8, -6e-8, 65504.0, -65504.0,
+                         1.0, -1.0, 3.5], dtype=torch.float16)
+    R, C = 24, 64
+    x = vals[torch.arange(R * C) % len(vals)].reshape(R, C)
+    y = vals[(torch.arange(R * C) * 7 + 3) % len(vals)].reshape(R, C)
+    body = [{"op": "relu", "operands": ["a0"]}, {"op": "scale", "operands": ["t0"], "factor": -1.5},
+            {"op": "add", "operands": ["t1", "a1"]}, {"op": "mul", "operands": ["t2", "a0"]}]
+    desc = kernels.chain_descriptor(2, body)
+    n0 = fpkern.chain_jit_launches()
+    out = fpkern.chain([x.cuda(), y.cuda()], desc, [R, C], torch.float32)
+    assert fpkern.chain_jit_launches() == n0 + 1
+    ops, res = oracle.body_to_program(2, body)
+    ref = oracle.chain_flat([x.numpy(), y.numpy()], ops, res, (R, C), np.float32)
+    o = out.cpu().numpy()
+    assert np.array_equal(np.isnan(o), np.isnan(ref))
+    np.testing.assert_array_equal(np.where(np.isnan(o), 0, o).view(np.int32), np.where(np.isnan(ref), 0, ref).view(np.int32))
+
+
+def test_jit_inside_cuda_graph_after_warmup():
+    R, C = 512, 1024
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(R, C, generator=g).half().cuda()
+    b = torch.randn(C, generator=g).half().cuda()
+    body = [{"op": "add", "operands": ["a0", "a1"]}, {"op": "gelu", "operands": ["t0"]}]
+    desc = kernels.chain_descriptor(2, body, input_bcast=["full", "col"])
+    out = torch.empty(R, C, dtype=torch.float16, device="cuda")
+    fpkern.chain([x, b], desc, [R, C], torch.float16, out=out)  # compiles and loads
+    ref = out.clone()
+    out.zero_()
+    torch.cuda.synchronize()
+    n0 = fpkern.chain_jit_launches()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fpkern.chain([x, b], desc, [R, C], torch.float16, out=out)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert fpkern.chain_jit_launches() == n0 + 1
+    assert torch.equal(out, ref)
+    del graph
+
+
+def test_first_use_under_capture_runs_the_interpreter():
+    """A chain first seen while a stream is capturing is served by the prebuilt
+    kernels (no module load inside a capture); the result is the same."""
+    R, C = 64, 256
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(R, C, generator=g).half().cuda()
+    body = [{"op": "scale", "operands": ["a0"], "factor": 0.731}, {"op": "exp", "operands": ["t0"]},
+            {"op": "mul", "operands": ["t1", "a0"]}]
+    desc = kernels.chain_descriptor(1, body)
+    out = torch.empty(R, C, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fpkern.chain([x], desc, [R, C], torch.float32, out=out)
+    graph.replay()
+    torch.cuda.synchronize()
+    ref = fpkern.chain([x], desc, [R, C], torch.float32, flags=_lib.FPK_FLAG_NO_JIT)
+    assert torch.equal(_bits(out), _bits(ref))
+    del graph

@@ -99,11 +99,13 @@ def _cfg2_inputs(R, C, seed=0):
 
 @pytest.mark.parametrize("R,C", [(4096, 4096), (1, 8), (3, 12), (257, 4100), (7, 3), (33, 8192), (19, 5000),
                                  (1000, 16), (5, 768), (64, 3072), (3, 8200)])
-@pytest.mark.parametrize("staging", [True, False])
-def test_cfg2_chain_vs_oracle_bit_exact(R, C, staging):
+@pytest.mark.parametrize("path", ["jit", "tiled", "general"])
+def test_cfg2_chain_vs_oracle_bit_exact(R, C, path):
+    """All three flat-chain tiers: run-time compiled (cols % 8 == 0), the row-tiled
+    interpreter and the general interpreter."""
     x, b, s = _cfg2_inputs(R, C)
     desc = kernels.chain_descriptor(3, CFG2_BODY, input_bcast=["full", "col", "col"])
-    flags = 0 if staging else _lib.FPK_FLAG_NO_STAGING
+    flags = {"jit": 0, "tiled": _lib.FPK_FLAG_NO_JIT, "general": _lib.FPK_FLAG_NO_STAGING}[path]
     out = fpkern.chain([x.cuda(), b.cuda(), s.cuda()], desc, [R, C], torch.float16, flags=flags)
     ops, res = oracle.body_to_program(3, CFG2_BODY)
     ref = oracle.chain_flat([x.numpy(), b.numpy(), s.numpy()], ops, res, (R, C), np.float16)
