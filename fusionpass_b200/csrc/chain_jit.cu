@@ -43,8 +43,11 @@ static const char kOpsSrc[] =
     ;
 
 constexpr int kVec = 8;        // elements per thread-vector
-constexpr int kBlock = 256;    // threads per CTA of the generated kernel
-constexpr int kCtasPerSm = 8;  // 2048 resident threads per SM
+// 64-thread CTAs, 16 per SM (1024 threads per SM, each with two 16-byte vectors
+// per full operand in flight): the fastest of the shapes measured on B200 for a
+// 4096 x 4096 f16 chain (13.6 us vs 14.7 us for 256 x 8 and 16 us for 1024 x 2).
+constexpr int kBlock = 64;      // threads per CTA of the generated kernel
+constexpr int kCtasPerSm = 16;  // CTAs per SM in the grid-stride launch
 
 struct JitParams {
   const void* in[FPK_CHAIN_MAX_INPUTS];
