@@ -122,7 +122,8 @@ static std::string gen_source(const fpk_chain_desc* d) {
   s += R"SRC(
 struct JitParams { const void* in[8]; void* out; i64 rows, cols, ncv, nvec; };
 __device__ __forceinline__ float h2f(u16 h) { float f; asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h)); return f; }
-__device__ __forceinline__ u32 f2h(float f) { u16 h; asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(f)); return h; }
+// f32 pair -> f16x2 in one instruction (lo in the low half), round to nearest even
+__device__ __forceinline__ u32 f2h2(float lo, float hi) { u32 r; asm("cvt.rn.f16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(lo), "f"(hi)); return r; }
 __device__ __forceinline__ void unpack8(uint4 u, float* a) {
   a[0] = h2f((u16)(u.x & 0xffffu)); a[1] = h2f((u16)(u.x >> 16));
   a[2] = h2f((u16)(u.y & 0xffffu)); a[3] = h2f((u16)(u.y >> 16));
@@ -151,8 +152,7 @@ __device__ __forceinline__ float ld1_f16(const void* b, i64 i) { return h2f(__ld
 __device__ __forceinline__ float ld1_f32(const void* b, i64 i) { return __ldg(reinterpret_cast<const float*>(b) + i); }
 __device__ __forceinline__ void st8_f16(void* b, i64 off, const float* y) {
   uint4 u;
-  u.x = f2h(y[0]) | (f2h(y[1]) << 16); u.y = f2h(y[2]) | (f2h(y[3]) << 16);
-  u.z = f2h(y[4]) | (f2h(y[5]) << 16); u.w = f2h(y[6]) | (f2h(y[7]) << 16);
+  u.x = f2h2(y[0], y[1]); u.y = f2h2(y[2], y[3]); u.z = f2h2(y[4], y[5]); u.w = f2h2(y[6], y[7]);
   __stcs(reinterpret_cast<uint4*>(reinterpret_cast<u16*>(b) + off), u);
 }
 __device__ __forceinline__ void st8_f32(void* b, i64 off, const float* y) {
