@@ -212,6 +212,104 @@ def weak_rate(world: int, steps: int, units_per_step: float, ms_max: float) -> f
     return world * steps * units_per_step / (ms_max * 1e-3)
 
 
+# ----------------------------------------------------- the other configs
+def _graph_time_ms(fn, reps: int, group: "RankGroup", stream) -> float:
+    """Max over ranks of the device time of `reps` calls of fn replayed from one CUDA graph."""
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=torch.cuda.Stream(group.device)):
+        for _ in range(reps):
+            fn()
+    g.replay()
+    group.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    g.replay()
+    e1.record(stream)
+    group.barrier()
+    ms = group.max(e0.elapsed_time(e1))
+    del g
+    return ms
+
+
+def run_configs(args, group: "RankGroup", rank: int, world: int, dev) -> dict:
+    """cfg1 (f32 attention demo), cfg4 (long-sequence D=128 attention) and cfg5
+    (BERT-base encoder block through the plan executor), each checked before it is
+    timed; weak scaling over ranks like the headline."""
+    from fusionpass_b200 import fpkern
+    from fusionpass_b200.api import compile_model
+
+    from oracle import attention as oa
+
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+
+    # cfg1: B1 H4 S128 D64 f32, Q/K/V ~ N(0,1) from seed 0, scale 1/8
+    g = torch.Generator().manual_seed(0)
+    q1, k1, v1 = (torch.randn(1, 4, 128, 64, generator=g) for _ in range(3))
+    qd, kd, vd = (t.to(dev) for t in (q1, k1, v1))
+    od = fpkern.attention(qd, kd, vd, 0.125)
+    ref = oa.attention_fwd(q1.numpy(), k1.numpy(), v1.numpy(), 0.125)
+    err = float(np.abs(od.cpu().numpy() - ref).max())
+    if not group.all_ok(err <= 1e-5):
+        raise RuntimeError(f"cfg1 attention differs from the oracle (max err {err:.2e})")
+    reps = 200
+    ms = _graph_time_ms(lambda: fpkern.attention(qd, kd, vd, 0.125, out=od), reps, group, stream)
+    flop = 4 * 1 * 4 * 128 * 128 * 64
+    out["cfg1_attention_f32"] = {"workload": "fp_attention B1 H4 S128 D64 f32, scale 1/8", "check": f"max err {err:.1e} vs oracle",
+                                 "us_per_launch": round(ms / reps * 1e3, 2),
+                                 "value": round(weak_rate(world, reps, flop, ms) / 1e12, 3), "unit": "TFLOP/s"}
+
+    # cfg4: B4 H32 S8192 D128 f16, Q/K/V ~ N(0,1), scale 1/sqrt(128)
+    if not args.no_long:
+        g = torch.Generator(device=dev).manual_seed(4000 + rank)
+        shp = (4, 32, 8192, 128)
+        q4, k4, v4 = (torch.randn(shp, generator=g, device=dev).half() for _ in range(3))
+        sc = 128 ** -0.5
+        o4 = fpkern.attention(q4, k4, v4, sc)
+        worst = 0.0
+        for b, h in ((0, 0), (3, 31)):
+            r = torch.softmax((q4[b, h].float() @ k4[b, h].float().T) * sc, -1) @ v4[b, h].float()
+            worst = max(worst, float(((o4[b, h].float() - r).abs() / (2e-3 + 1e-2 * r.abs())).max()))
+        if not group.all_ok(worst <= 1.0):
+            raise RuntimeError(f"cfg4 attention outside the f16 tolerance ({worst:.2f} of it)")
+        reps = 5
+        ms = _graph_time_ms(lambda: fpkern.attention(q4, k4, v4, sc, out=o4), reps, group, stream)
+        flop = 4 * 4 * 32 * 8192 ** 2 * 128
+        tf = flop / (ms / reps * 1e-3) / 1e12
+        out["cfg4_attention_long"] = {
+            "workload": "fp_attention B4 H32 S8192 D128 f16, scale 1/sqrt(128)",
+            "check": f"2 (b,h) slices vs torch f32: {worst:.2f} of the atol 2e-3 / rtol 1e-2 budget",
+            "ms_per_launch": round(ms / reps, 3), "value": round(weak_rate(world, reps, flop, ms) / 1e12, 2),
+            "unit": "TFLOP/s", "roofline_frac": round(tf / peaks()["tc"], 4)}
+        del q4, k4, v4, o4
+
+    # cfg5: BERT-base block, batch 32 seq 512 hidden 768 heads 12 FFN 3072, f16
+    if not args.no_bert:
+        sys.path.insert(0, str(ROOT))
+        from tests.models import BertBlock, init_bert
+
+        torch.manual_seed(0)
+        m = init_bert(BertBlock(32, 512)).half().to(dev).eval()
+        g = torch.Generator(device=dev).manual_seed(5000 + rank)
+        x = torch.randn(32, 512, 768, generator=g, device=dev).half()
+        c = compile_model(m, (x,), fuse=True, extensions=True, strict=False)
+        kinds = [st.get("launch", st["kind"]) for st in c.plan["steps"]]
+        if not group.all_ok(bool(c.verified)):
+            raise RuntimeError(f"cfg5 BERT block failed the equivalence gate: {c.report}")
+        reps = 20
+        with torch.no_grad():
+            ms = _graph_time_ms(lambda: c(x), reps, group, stream)
+        tokens = 32 * 512
+        out["cfg5_bert_block"] = {
+            "workload": "BERT-base encoder block f16, batch 32 seq 512 hidden 768 heads 12 FFN 3072 (random init)",
+            "check": "verify_equivalence gate passed (f16 1e-2 / 1e-2, 3 trials)",
+            "fused_steps": {"attention": kinds.count("attention"), "flat_chains": kinds.count("flat")},
+            "ms_per_block": round(ms / reps, 4), "value": round(weak_rate(world, reps, tokens, ms), 1),
+            "unit": "tokens/s",
+            "note": "whole block through execute_plan; Linear/LayerNorm run as unfused torch steps"}
+    return out
+
+
 def run_ours(args, rank, world, dev):
     from fusionpass_b200 import fpkern, kernels
     from fusionpass_b200.runtime import execute_plan
@@ -349,6 +447,7 @@ def run_ours(args, rank, world, dev):
         del ag
 
     del graph
+    configs = None if args.no_configs else run_configs(args, group, rank, world, dev)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
@@ -374,7 +473,7 @@ def run_ours(args, rank, world, dev):
                      "frac_of_spec_8000": round(chain_gbs / 8000.0, 4),
                      "traffic": traffic.get("chain_cfg2", {}).get("dram_bytes_per_launch"),
                      "algorithmic_bytes_per_launch": CHAIN_BYTES},
-        "clocks": clocks, "gpu_launches": K, "e2e": e2e, "cpu_baseline": cpu, "attention": attention,
+        "clocks": clocks, "gpu_launches": K, "e2e": e2e, "cpu_baseline": cpu, "attention": attention, "configs": configs,
         "impl": "ours",
     }
     return line
@@ -434,6 +533,9 @@ def main(argv=None) -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--skip-check", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the cfg1/cfg4/cfg5 entries")
+    ap.add_argument("--no-long", action="store_true", help="skip the cfg4 entry")
+    ap.add_argument("--no-bert", action="store_true", help="skip the cfg5 entry")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
