@@ -357,14 +357,18 @@ __device__ __forceinline__ void drain_wait_w(uint64_t* bar, uint32_t parity, int
 
 template <int N>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t* r) {
-  if constexpr (N == 16) tmem_ld_x16(taddr, r);
+  static_assert(N == 8 || N == 16 || N == 32 || N == 64 || N == 128, "no tcgen05.ld form for this width");
+  if constexpr (N == 8) tmem_ld_x8(taddr, r);
+  else if constexpr (N == 16) tmem_ld_x16(taddr, r);
   else if constexpr (N == 32) tmem_ld_x32(taddr, r);
   else if constexpr (N == 64) tmem_ld_x64(taddr, r);
   else tmem_ld_x128(taddr, r);
 }
 template <int N>
 __device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t* r) {
-  if constexpr (N == 16) tmem_st_x16(taddr, r);
+  static_assert(N == 8 || N == 16 || N == 32 || N == 64 || N == 128, "no tcgen05.st form for this width");
+  if constexpr (N == 8) tmem_st_x8(taddr, r);
+  else if constexpr (N == 16) tmem_st_x16(taddr, r);
   else if constexpr (N == 32) tmem_st_x32(taddr, r);
   else if constexpr (N == 64) tmem_st_x64(taddr, r);
   else tmem_st_x128(taddr, r);
