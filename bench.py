@@ -554,26 +554,28 @@ def main(argv=None) -> int:
         return 1
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world > 1:
-        import datetime
-
-        import torch.distributed as tdist
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    # stdout carries exactly one JSON line: library output during the run (the NCCL
-    # version banner, for one) goes to stderr
+    # stdout carries exactly one JSON line: library output from process-group setup to
+    # teardown (the NCCL version banner, for one) goes to stderr
     sys.stdout.flush()
     saved = os.dup(1)
     os.dup2(2, 1)
     try:
-        line = run_ours(args, rank, world, dev)
+        if world > 1:
+            import datetime
+
+            import torch.distributed as tdist
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        try:
+            line = run_ours(args, rank, world, dev)
+        finally:
+            if world > 1:
+                import torch.distributed as tdist
+                tdist.destroy_process_group()
     finally:
         sys.stdout.flush()
         os.dup2(saved, 1)
         os.close(saved)
-        if world > 1:
-            import torch.distributed as tdist
-            tdist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
