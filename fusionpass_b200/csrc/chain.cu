@@ -1446,6 +1446,8 @@ int launch_chain(const fpk_chain_desc* d, const void* const* inputs, void* out, 
   }
 
   if (prog.softmax_pc < 0) return FPK_ERR_INVALID;
+  rc = try_launch_chain_jit(d, inputs, out, stream, dev);
+  if (rc != FPK_ERR_UNSUPPORTED) return rc;
   p.n_pre = prog.softmax_pc;
   for (int pc = prog.softmax_pc + 1; pc < prog.n; ++pc) {
     const int c = prog.code[pc];

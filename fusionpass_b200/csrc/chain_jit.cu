@@ -26,6 +26,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <algorithm>
 #include <atomic>
 #include <cstring>
 #include <mutex>
@@ -90,17 +91,44 @@ static const Nvrtc& nvrtc() {
 }
 
 // ------------------------------------------------------- source generator ---
-// Eligibility that depends on the descriptor alone.
-static bool shape_ok(const fpk_chain_desc* d) {
-  if (d->mode != FPK_CHAIN_FLAT || d->cols <= 0 || d->rows <= 0 || d->cols % kVec) return false;
-  if (d->flags & (FPK_FLAG_TEST_TIMEOUT | FPK_FLAG_NO_STAGING | FPK_FLAG_NO_JIT)) return false;
+// Which generated kernel (if any) takes `d`: eligibility that depends on the
+// descriptor alone (pointer alignment is checked at launch).
+enum JitKind { kNone = 0, kFlat = 1, kRows = 2 };
+constexpr int kRowsMaxCols = 16384;
+
+static JitKind jit_kind(const fpk_chain_desc* d) {
+  if (d->cols <= 0 || d->rows <= 0 || d->cols % kVec) return kNone;
+  if (d->flags & (FPK_FLAG_TEST_TIMEOUT | FPK_FLAG_NO_STAGING | FPK_FLAG_NO_JIT)) return kNone;
+  int softmax = 0;
   for (int k = 0; k < d->n_ops; ++k) {
     const int op = d->ops[k].opcode;
+    if (op == FPK_OP_SOFTMAX) {
+      ++softmax;
+      continue;
+    }
     if (op != FPK_OP_ADD && op != FPK_OP_MUL && op != FPK_OP_SCALE && op != FPK_OP_RELU && op != FPK_OP_EXP &&
         op != FPK_OP_GELU)
-      return false;
+      return kNone;
   }
-  return true;
+  if (d->mode == FPK_CHAIN_FLAT) return softmax == 0 ? kFlat : kNone;
+  if (d->mode == FPK_CHAIN_ROWS && softmax == 1 && d->cols <= kRowsMaxCols) return kRows;
+  return kNone;
+}
+
+// Rows kernel geometry, fixed by the column count: TPR threads share a row, each
+// holding VPT 8-element vectors (vector v of the row at thread v % TPR, slot v / TPR).
+struct RowsGeom {
+  int nv, tpr, vpt, block, rows_per_cta;
+};
+static RowsGeom rows_geom(long long cols) {
+  RowsGeom g;
+  g.nv = static_cast<int>(cols / kVec);
+  auto pow2 = [](int n) { int p = 1; while (p < n) p <<= 1; return p; };
+  g.tpr = g.nv <= 32 ? pow2(g.nv) : std::min(512, pow2((g.nv + 3) / 4));
+  g.vpt = (g.nv + g.tpr - 1) / g.tpr;
+  g.block = g.tpr > 256 ? g.tpr : 256;
+  g.rows_per_cta = g.block / g.tpr;
+  return g;
 }
 
 static void app(std::string& s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
@@ -113,10 +141,9 @@ static void app(std::string& s, const char* fmt, ...) {
   if (n > 0) s.append(buf, static_cast<size_t>(n < static_cast<int>(sizeof(buf)) ? n : sizeof(buf) - 1));
 }
 
-static std::string gen_source(const fpk_chain_desc* d) {
-  const int nin = d->n_inputs;
-  std::string s;
-  s.reserve(8192);
+// Types, the shared op definitions and the load / store helpers of every generated kernel.
+static void prelude(std::string& s) {
+  s.reserve(16384);
   s += "typedef unsigned int u32;\ntypedef unsigned short u16;\ntypedef long long i64;\n";
   s += kOpsSrc;
   s += R"SRC(
@@ -161,6 +188,12 @@ __device__ __forceinline__ void st8_f32(void* b, i64 off, const float* y) {
   __stcs(p + 1, make_float4(y[4], y[5], y[6], y[7]));
 }
 )SRC";
+}
+
+static std::string gen_flat_source(const fpk_chain_desc* d) {
+  const int nin = d->n_inputs;
+  std::string s;
+  prelude(s);
   const char* dt[2] = {"f32", "f16"};
   auto idt = [&](int i) { return dt[d->in_dtype[i] == FPK_F16 ? 1 : 0]; };
 
@@ -250,6 +283,104 @@ __device__ __forceinline__ void st8_f32(void* b, i64 off, const float* y) {
   return s;
 }
 
+// Rows mode: one last-axis softmax.  The column count is a compile-time
+// constant, so a row's values stay in registers: TPR threads share a row, each
+// loads its VPT vectors, evaluates the ops before the softmax, reduces the row
+// max and sum (shuffles within a warp, shared memory across the warps of a row),
+// then evaluates the ops after it and stores.  Softmax arithmetic as the
+// interpreter's: e = exp(x - max) (0 for masked columns), sum by round-to-nearest
+// adds, p = e / sum.
+static std::string gen_rows_source(const fpk_chain_desc* d) {
+  const int nin = d->n_inputs;
+  const RowsGeom g = rows_geom(d->cols);
+  const int E = g.vpt * kVec;  // elements per thread
+  const int wpr = g.tpr > 32 ? g.tpr / 32 : 1;  // warps per row
+  std::string s;
+  prelude(s);
+  const char* dt[2] = {"f32", "f16"};
+  auto idt = [&](int i) { return dt[d->in_dtype[i] == FPK_F16 ? 1 : 0]; };
+  int ksm = -1;
+  for (int k = 0; k < d->n_ops; ++k)
+    if (d->ops[k].opcode == FPK_OP_SOFTMAX) ksm = k;
+
+  app(s, "#define TPR %d\n#define VPT %d\n#define NV %d\n#define E %d\n#define WPR %d\n#define RPC %d\n", g.tpr, g.vpt,
+      g.nv, E, wpr, g.rows_per_cta);
+  s += "#define INFINITY __int_as_float(0x7f800000)\n";
+  app(s, "extern \"C\" __global__ void __launch_bounds__(%d) fpk_jit_chain(const JitParams p) {\n", g.block);
+  s += "  const int t = threadIdx.x % TPR, rl = threadIdx.x / TPR;\n";
+  s += "  const i64 row = (i64)blockIdx.x * RPC + rl;\n";
+  s += "  const bool live = row < p.rows;  // every thread takes part in the reductions\n";
+  s += "  const i64 base = (live ? row : 0) * p.cols;\n";
+  if (wpr > 1) s += "  __shared__ float red[2][RPC][WPR];\n";
+  // input values
+  for (int i = 0; i < nin; ++i) {
+    const int b = d->in_bcast[i];
+    if (b == FPK_BCAST_FULL || b == FPK_BCAST_COL) {
+      app(s, "  float v%d[E];\n", i);
+      app(s, "  #pragma unroll\n  for (int k = 0; k < VPT; ++k) {\n    const int vv = k * TPR + t;\n");
+      if (b == FPK_BCAST_FULL)
+        app(s, "    if (live && vv < NV) ld8s_%s(p.in[%d], base + vv * 8, v%d + k * 8);\n", idt(i), i, i);
+      else
+        app(s, "    if (vv < NV) ld8c_%s(p.in[%d], vv * 8, v%d + k * 8);\n", idt(i), i, i);
+      app(s, "    else { for (int e = 0; e < 8; ++e) v%d[k * 8 + e] = 0.0f; }\n  }\n", i);
+    } else if (b == FPK_BCAST_ROW) {
+      app(s, "  const float r%d = live ? ld1_%s(p.in[%d], row) : 0.0f;\n  float v%d[E];\n", i, idt(i), i, i);
+      app(s, "  #pragma unroll\n  for (int e = 0; e < E; ++e) v%d[e] = r%d;\n", i, i);
+    } else {
+      app(s, "  const float s%d = ld1_%s(p.in[%d], 0);\n  float v%d[E];\n", i, idt(i), i, i);
+      app(s, "  #pragma unroll\n  for (int e = 0; e < E; ++e) v%d[e] = s%d;\n", i, i);
+    }
+  }
+  auto emit_op = [&](int k) {
+    const fpk_chain_op& op = d->ops[k];
+    const int dst = nin + k;
+    app(s, "  float v%d[E];\n  #pragma unroll\n  for (int e = 0; e < E; ++e) ", dst);
+    switch (op.opcode) {
+      case FPK_OP_ADD: app(s, "v%d[e] = __fadd_rn(v%d[e], v%d[e]);\n", dst, op.src_a, op.src_b); break;
+      case FPK_OP_MUL: app(s, "v%d[e] = __fmul_rn(v%d[e], v%d[e]);\n", dst, op.src_a, op.src_b); break;
+      case FPK_OP_SCALE: {
+        uint32_t bits;
+        std::memcpy(&bits, &op.imm, 4);
+        app(s, "v%d[e] = __fmul_rn(v%d[e], __uint_as_float(0x%08xu));\n", dst, op.src_a, bits);
+        break;
+      }
+      case FPK_OP_RELU: app(s, "v%d[e] = op_relu(v%d[e]);\n", dst, op.src_a); break;
+      case FPK_OP_EXP: app(s, "v%d[e] = expf(v%d[e]);\n", dst, op.src_a); break;
+      default: app(s, "v%d[e] = op_gelu(v%d[e]);\n", dst, op.src_a); break;
+    }
+  };
+  for (int k = 0; k < ksm; ++k) emit_op(k);
+  // the softmax
+  const int src = d->ops[ksm].src_a, dst = nin + ksm;
+  auto valid = "(((e >> 3) * TPR + t) < NV)";
+  app(s, "  float m = -INFINITY;\n  #pragma unroll\n  for (int e = 0; e < E; ++e) if (%s) m = fmaxf(m, v%d[e]);\n",
+      valid, src);
+  app(s, "  #pragma unroll\n  for (int off = (TPR < 32 ? TPR : 32) / 2; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));\n");
+  if (wpr > 1) {
+    s += "  if ((threadIdx.x & 31) == 0) red[0][rl][t >> 5] = m;\n  __syncthreads();\n";
+    s += "  m = red[0][rl][0];\n  #pragma unroll\n  for (int w = 1; w < WPR; ++w) m = fmaxf(m, red[0][rl][w]);\n";
+  }
+  app(s, "  float ev[E];\n  float sum = 0.0f;\n  #pragma unroll\n  for (int e = 0; e < E; ++e) {\n"
+         "    const float x = %s ? v%d[e] : -INFINITY;\n"
+         "    ev[e] = (x == -INFINITY) ? 0.0f : expf(__fsub_rn(x, m));\n    sum = __fadd_rn(sum, ev[e]);\n  }\n",
+      valid, src);
+  app(s, "  #pragma unroll\n  for (int off = (TPR < 32 ? TPR : 32) / 2; off > 0; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));\n");
+  if (wpr > 1) {
+    s += "  if ((threadIdx.x & 31) == 0) red[1][rl][t >> 5] = sum;\n  __syncthreads();\n";
+    s += "  sum = red[1][rl][0];\n  #pragma unroll\n  for (int w = 1; w < WPR; ++w) sum = __fadd_rn(sum, red[1][rl][w]);\n";
+  }
+  app(s, "  float v%d[E];\n  #pragma unroll\n  for (int e = 0; e < E; ++e) v%d[e] = __fdiv_rn(ev[e], sum);\n", dst, dst);
+  for (int k = ksm + 1; k < d->n_ops; ++k) emit_op(k);
+  app(s, "  if (live) {\n  #pragma unroll\n  for (int k = 0; k < VPT; ++k) {\n    const int vv = k * TPR + t;\n"
+         "    if (vv < NV) st8_%s(p.out, base + vv * 8, v%d + k * 8);\n  }\n  }\n}\n",
+      d->out_dtype == FPK_F16 ? "f16" : "f32", d->result);
+  return s;
+}
+
+static std::string gen_source(const fpk_chain_desc* d, JitKind kind) {
+  return kind == kRows ? gen_rows_source(d) : gen_flat_source(d);
+}
+
 // ------------------------------------------------------------------ cache ---
 struct Entry {
   std::vector<char> cubin;
@@ -299,8 +430,9 @@ static bool compile_locked(const std::string& src, Entry& e) {
 
 int chain_jit_precompile(const fpk_chain_desc* d) {
   using namespace chain_jit;
-  if (!shape_ok(d)) return FPK_ERR_UNSUPPORTED;
-  const std::string src = gen_source(d);
+  const JitKind kind = jit_kind(d);
+  if (kind == kNone) return FPK_ERR_UNSUPPORTED;
+  const std::string src = gen_source(d, kind);
   std::lock_guard<std::mutex> lk(g_mu);
   Entry& e = cache()[src];
   if (e.failed) return FPK_ERR_UNSUPPORTED;
@@ -315,14 +447,15 @@ int chain_jit_precompile(const fpk_chain_desc* d) {
 int try_launch_chain_jit(const fpk_chain_desc* d, const void* const* inputs, void* out, cudaStream_t stream,
                          const DeviceInfo& dev) {
   using namespace chain_jit;
-  if (!shape_ok(d)) return FPK_ERR_UNSUPPORTED;
+  const JitKind kind = jit_kind(d);
+  if (kind == kNone) return FPK_ERR_UNSUPPORTED;
   if (reinterpret_cast<uintptr_t>(out) % 16) return FPK_ERR_UNSUPPORTED;
   for (int i = 0; i < d->n_inputs; ++i) {
     const int b = d->in_bcast[i];
     if ((b == FPK_BCAST_FULL || b == FPK_BCAST_COL) && reinterpret_cast<uintptr_t>(inputs[i]) % 16)
       return FPK_ERR_UNSUPPORTED;
   }
-  const std::string src = gen_source(d);
+  const std::string src = gen_source(d, kind);
   cudaKernel_t kern = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -356,12 +489,22 @@ int try_launch_chain_jit(const fpk_chain_desc* d, const void* const* inputs, voi
   p.cols = d->cols;
   p.ncv = d->cols / kVec;
   p.nvec = d->rows * p.ncv;
-  const long long per_cta = static_cast<long long>(kBlock) * 2;  // two vectors per thread and step
-  long long grid = (p.nvec + per_cta - 1) / per_cta;
-  const long long cap = static_cast<long long>(dev.num_sms > 0 ? dev.num_sms : 148) * kCtasPerSm;
-  if (grid > cap) grid = cap;
+  long long grid;
+  int block;
+  if (kind == kRows) {
+    const RowsGeom g = rows_geom(d->cols);
+    grid = (d->rows + g.rows_per_cta - 1) / g.rows_per_cta;  // one row per TPR-thread group
+    block = g.block;
+    if (grid > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
+  } else {
+    const long long per_cta = static_cast<long long>(kBlock) * 2;  // two vectors per thread and step
+    grid = (p.nvec + per_cta - 1) / per_cta;
+    const long long cap = static_cast<long long>(dev.num_sms > 0 ? dev.num_sms : 148) * kCtasPerSm;
+    if (grid > cap) grid = cap;
+    block = kBlock;
+  }
   void* args[] = {&p};
-  if (cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(static_cast<unsigned>(grid)), dim3(kBlock), args, 0,
+  if (cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(static_cast<unsigned>(grid)), dim3(block), args, 0,
                        stream) != cudaSuccess)
     return FPK_ERR_CUDA;
   g_launches.fetch_add(1, std::memory_order_relaxed);

@@ -53,8 +53,9 @@ extern "C" {
 #define FPK_FLAG_TEST_TIMEOUT 0x1u
 /* Chain only: read every operand with plain loads (no TMA bulk staging). */
 #define FPK_FLAG_NO_STAGING   0x2u
-/* Flat chains: skip the per-program kernel compiled at run time and run the
- * prebuilt interpreter kernels (both give identical bits; tests compare them). */
+/* Chains: skip the per-program kernel compiled at run time and run the prebuilt
+ * interpreter kernels (flat chains: identical bits; rows: the same arithmetic
+ * with another summation order; tests compare them). */
 #define FPK_FLAG_NO_JIT       0x4u
 
 /* ---- attention: O = softmax(scale * Q K^T) V, per (batch, head) ---------- */
@@ -144,19 +145,19 @@ int fpk_attention_fwd(const fpk_attn_desc* d, const void* q, const void* k,
 int fpk_chain_fwd(const fpk_chain_desc* d, const void* const* inputs, int n_inputs,
                   void* out, void* stream);
 
-/* Compile (and cache for the process) the per-program kernel of a flat chain
+/* Compile (and cache for the process) the per-program kernel of a chain
  * without launching it, as the first fpk_chain_fwd with this op list, operand
- * types and broadcast modes would.  Needs no device.  FPK_OK, or
- * FPK_ERR_UNSUPPORTED when the chain is not one this tier compiles (rows mode,
- * cols % 8 != 0, FPK_FLAG_NO_JIT / NO_STAGING / TEST_TIMEOUT) or no run-time
- * compiler (libnvrtc.so.12) is available -- fpk_chain_fwd then runs the
- * prebuilt kernels.  Counterpart of the reference's kernel warm-up: Triton
+ * types and broadcast modes (and, in rows mode, column count) would.  Needs no
+ * device.  FPK_OK, or FPK_ERR_UNSUPPORTED when the chain is not one this tier
+ * compiles (cols % 8 != 0, rows mode with cols > 16384, FPK_FLAG_NO_JIT /
+ * NO_STAGING / TEST_TIMEOUT) or no run-time compiler (libnvrtc.so.12) is
+ * available -- fpk_chain_fwd then runs the prebuilt kernels.  Counterpart of the reference's kernel warm-up: Triton
  * compiles each fp_chain_<N> at its first launch (python/fusionpass/kernels.py:
  * 288-300). */
 int fpk_chain_precompile(const fpk_chain_desc* d);
 
-/* Diagnostic, no reference counterpart: the number of flat chains this process
- * has launched through run-time compiled kernels (the rest ran on the prebuilt
+/* Diagnostic, no reference counterpart: the number of chains this process has
+ * launched through run-time compiled kernels (the rest ran on the prebuilt
  * interpreter kernels). */
 int64_t fpk_chain_jit_launches(void);
 

@@ -7,7 +7,7 @@ import torch
 
 import oracle
 from fusionpass_b200 import _lib, fpkern, kernels
-from tests.test_chain_jit_cpu import random_chain
+from tests.test_chain_jit_cpu import random_chain, random_rows_chain
 
 pytestmark = pytest.mark.gpu
 
@@ -115,3 +115,62 @@ def test_first_use_under_capture_runs_the_interpreter():
     ref = fpkern.chain([x], desc, [R, C], torch.float32, flags=_lib.FPK_FLAG_NO_JIT)
     assert torch.equal(_bits(out), _bits(ref))
     del graph
+
+
+def _allclose(a, b, dt):
+    a, b = a.float().cpu().numpy(), b.float().cpu().numpy()
+    if dt == torch.float16:
+        np.testing.assert_allclose(a, b, rtol=1e-2, atol=2e-3, equal_nan=True)
+    else:
+        np.testing.assert_allclose(a, b, rtol=2e-5, atol=1e-6, equal_nan=True)
+
+
+@pytest.mark.parametrize("seed", range(4))
+@pytest.mark.parametrize("R,C", [(1, 8), (37, 40), (300, 128), (64, 1000), (33, 1024), (17, 4096), (5, 16384)])
+def test_random_rows_programs_jit_vs_interpreter(seed, R, C):
+    """Rows mode: the compiled kernel reduces in another order than the interpreter, so the
+    two agree within rounding (and both within tolerance of the oracle elsewhere)."""
+    rng = np.random.default_rng(200 + seed)
+    g = torch.Generator().manual_seed(seed)
+    n_in = int(rng.integers(1, 4))
+    body = random_rows_chain(rng, n_in)
+    bc = ["full"] + [["full", "col", "row", "scalar"][int(rng.integers(4))] for _ in range(n_in - 1)]
+    dts = [[torch.float16, torch.float32][int(rng.integers(2))] for _ in range(n_in)]
+    out_dt = [torch.float16, torch.float32][int(rng.integers(2))]
+    desc = kernels.chain_descriptor(n_in, body, input_bcast=bc)
+    ins = [_operand(k, R, C, dt, g) for k, dt in zip(bc, dts)]
+    n0 = fpkern.chain_jit_launches()
+    y_jit = fpkern.chain(ins, desc, [R, C], out_dt)
+    assert fpkern.chain_jit_launches() == n0 + 1, "the run-time compiled rows kernel did not run"
+    y_int = fpkern.chain(ins, desc, [R, C], out_dt, flags=_lib.FPK_FLAG_NO_JIT)
+    assert fpkern.chain_jit_launches() == n0 + 1
+    _allclose(y_jit, y_int, out_dt)
+
+
+@pytest.mark.parametrize("C", [8, 128, 1000, 4096, 16384])
+def test_rows_softmax_jit_vs_oracle(C):
+    R = 24
+    g = torch.Generator().manual_seed(C)
+    x = (torch.randn(R, C, generator=g) * 4).float()
+    b = torch.randn(C, generator=g).float()
+    body = [{"op": "add", "operands": ["a0", "a1"]}, {"op": "softmax", "operands": ["t0"]},
+            {"op": "mul", "operands": ["t1", "a0"]}]
+    desc = kernels.chain_descriptor(2, body, input_bcast=["full", "col"])
+    n0 = fpkern.chain_jit_launches()
+    out = fpkern.chain([x.cuda(), b.cuda()], desc, [R, C], torch.float32)
+    assert fpkern.chain_jit_launches() == n0 + 1
+    ops, res = oracle.body_to_program(2, body)
+    ref = oracle.chain_rows([x.numpy(), np.broadcast_to(b.numpy(), (R, C))], ops, res, (R, C), np.float32)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-5, atol=1e-5)
+
+
+def test_rows_all_masked_like_values():
+    """A row of -inf scores gives NaN like the reference (exp(-inf - -inf)); others are fine."""
+    R, C = 4, 64
+    x = torch.randn(R, C)
+    x[1] = float("-inf")
+    desc = kernels.chain_descriptor(1, [{"op": "softmax", "operands": ["a0"]}])
+    out = fpkern.chain([x.cuda()], desc, [R, C], torch.float32).cpu()
+    ref = fpkern.chain([x.cuda()], desc, [R, C], torch.float32, flags=_lib.FPK_FLAG_NO_JIT).cpu()
+    assert torch.isnan(out[1]).all() and torch.isnan(ref[1]).all()
+    torch.testing.assert_close(out[[0, 2, 3]], torch.softmax(x[[0, 2, 3]], -1), rtol=1e-5, atol=1e-6)
