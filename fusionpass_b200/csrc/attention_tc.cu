@@ -70,7 +70,7 @@ static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsCtl <= kThreads * 168, "setmax
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;
 constexpr uint32_t kPolyPairs = 0x11u;  // pairs (c/2) mod 8 in {0, 4} use the FMA-pipe exp2
-constexpr int kTurnAt = 96;             // score column after which the exponential turn passes
+constexpr int kTurnAt = 104;            // score column after which the exponential turn passes
 constexpr int kMinSmem = 116 * 1024;  // keeps one CTA per SM (it owns all 512 TMEM columns)
 
 template <int D>
@@ -104,6 +104,7 @@ struct Bars {
   // p_full / turn: one arrival per softmax warp (lane 0 after __syncwarp)
   uint64_t s_full[kTiles], p_full[kTiles], o_done[kTiles];
   uint64_t turn[kTiles];    // ping-pong of the exponential phases of the two tiles
+  uint64_t epi[kTiles];     // the 4 warps of a tile before the O store (a bounded wait)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -421,6 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars.p_full[t], kWG / 32);
       mbar_init(&bars.o_done[t], 1);
       mbar_init(&bars.turn[t], kWG / 32);
+      mbar_init(&bars.epi[t], kWG / 32);
     }
     mbar_init(&bars.drain, 1);
     bars.abort = 0;
@@ -690,8 +692,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         fence_proxy_async_smem();
-        named_bar_sync(1 + t, kWG);
-        if (row == 0) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.epi[t]);
+        if (mbar_wait(&bars.epi[t], 0, abort, p.status, limit) && row == 0) {
           for (int bx = 0; bx < C::kBoxes; ++bx)
             tma_store_4d(&to, stage + bx * C::kBoxBytes, bx * C::kBoxCols, m0 + t * kBM, hh, bb);
         }
@@ -720,6 +723,7 @@ struct PBars {
   uint64_t q_full, q_empty;
   uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
   uint64_t s_full[kTiles], p_full[kTiles], o_done[kTiles], s_free[kTiles], turn[kTiles];
+  uint64_t epi[kTiles][2];  // the 4 warps of a tile, twice per epilogue (bounded waits)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -787,6 +791,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars.o_done[t], 1);
       mbar_init(&bars.s_free[t], kWG / 32);
       mbar_init(&bars.turn[t], kWG / 32);
+      mbar_init(&bars.epi[t][0], kWG / 32);
+      mbar_init(&bars.epi[t][1], kWG / 32);
     }
     mbar_init(&bars.drain, 1);
     bars.abort = 0;
@@ -989,6 +995,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* stage = sO + t * C::kTileBytes;
     uint32_t g = 0u;   // key iterations this tile has done (barrier phases)
     uint32_t tt = 0u;  // key iterations of two-tile items done (turn phases)
+    uint32_t ne = 0u;  // epilogues done (epi barrier phases)
     bool ok = true;
     for (int w = blockIdx.x; ok && w < total; w += gridDim.x) {
       int hh, bb, m0, ntiles;
@@ -1099,7 +1106,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&bars.o_done[t], (g - 1u) & 1u, abort, p.status, limit)) break;
       tc_fence_after();
       if (row == 0) bulk_wait_read_all();  // the previous store has read the staging buffer
-      named_bar_sync(1 + t, kWG);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.epi[t][0]);
+      if (!mbar_wait(&bars.epi[t][0], ne & 1u, abort, p.status, limit)) break;
       constexpr int kChunk = D < 32 ? D : 32;
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += kChunk) {
@@ -1120,7 +1129,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       fence_proxy_async_smem();
-      named_bar_sync(1 + t, kWG);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.epi[t][1]);
+      if (!mbar_wait(&bars.epi[t][1], ne & 1u, abort, p.status, limit)) break;
+      ++ne;
       if (row == 0) {
         for (int bx = 0; bx < C::kBoxes; ++bx)
           tma_store_4d_async(&to, stage + bx * C::kBoxBytes, bx * C::kBoxCols, m0 + t * kBM, hh, bb);
