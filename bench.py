@@ -151,6 +151,22 @@ def cpu_chain_rate(seconds: float, threads: int):
     return passes * CHAIN_BYTES / dt / 1e9, passes
 
 
+def cpu_eager_torch_rate(seconds: float, threads: int):
+    """Eager PyTorch on the host cores, the same module as the chain workload
+    (y = relu((x + b) * s) * 0.5 + x in f16): bytes of the workload per second."""
+    torch.set_num_threads(threads)
+    x, b, s = chain_inputs(0)
+    passes = 0
+    t0 = time.perf_counter()
+    while True:
+        torch.relu((x + b) * s) * 0.5 + x
+        passes += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return passes * CHAIN_BYTES / dt / 1e9, passes
+
+
 def cpu_attention_rate(seconds: float, threads: int):
     """The oracle restatement of fp_attention on B*H slices of the prefill workload."""
     from oracle import attention as oa
@@ -466,11 +482,15 @@ def run_ours(args, rank, world, dev):
     del graph
     configs = None if args.no_configs else run_configs(args, group, rank, world, dev)
     cpu = None
+    cpu_eager = None
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
         gbs, passes = cpu_chain_rate(args.cpu_seconds, threads)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": f"{passes} full passes of the [4096,4096] chain in 256-row blocks, numpy oracle"}
+        eg, ep = cpu_eager_torch_rate(min(args.cpu_seconds, 2.0), threads)
+        cpu_eager = {"value": round(eg, 3), "unit": "GB/s", "threads": threads,
+                     "sample": f"{ep} passes of the [4096,4096] f16 module in eager PyTorch on the CPU"}
         if attention is not None:
             tf, slices = cpu_attention_rate(args.cpu_seconds, threads)
             attention["cpu_baseline"] = {"value": round(tf, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
@@ -490,7 +510,8 @@ def run_ours(args, rank, world, dev):
                      "frac_of_spec_8000": round(chain_gbs / 8000.0, 4),
                      "traffic": traffic.get("chain_cfg2", {}).get("dram_bytes_per_launch"),
                      "algorithmic_bytes_per_launch": CHAIN_BYTES},
-        "clocks": clocks, "gpu_launches": K, "e2e": e2e, "cpu_baseline": cpu, "attention": attention, "configs": configs,
+        "clocks": clocks, "gpu_launches": K, "e2e": e2e, "cpu_baseline": cpu, "cpu_eager_torch": cpu_eager, "attention": attention,
+        "configs": configs,
         "impl": "ours",
     }
     return line

@@ -174,3 +174,37 @@ def test_rows_all_masked_like_values():
     ref = fpkern.chain([x.cuda()], desc, [R, C], torch.float32, flags=_lib.FPK_FLAG_NO_JIT).cpu()
     assert torch.isnan(out[1]).all() and torch.isnan(ref[1]).all()
     torch.testing.assert_close(out[[0, 2, 3]], torch.softmax(x[[0, 2, 3]], -1), rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("mode", ["flat", "rows"])
+def test_max_size_chain_jit_vs_interpreter(mode):
+    """8 operands (all broadcast modes, both dtypes) and 32 ops, the descriptor limits."""
+    rng = np.random.default_rng(31)
+    g = torch.Generator().manual_seed(31)
+    R, C = 96, 1024
+    n_in = _lib.FPK_CHAIN_MAX_INPUTS
+    bc = ["full", "col", "row", "scalar", "full", "col", "full", "row"]
+    dts = [torch.float16, torch.float32] * 4
+    names = [f"a{i}" for i in range(n_in)]
+    body = []
+    n_ops = _lib.FPK_CHAIN_MAX_OPS
+    for k in range(n_ops):
+        if mode == "rows" and k == 20:
+            body.append({"op": "softmax", "operands": [names[-1]]})
+        elif k % 4 == 3:
+            body.append({"op": "scale", "operands": [names[-1]], "factor": 0.5})
+        else:
+            op = ["add", "mul", "relu"][k % 3]
+            a, b = names[-1], names[int(rng.integers(n_in))]
+            body.append({"op": op, "operands": [a, b] if op != "relu" else [a]})
+        names.append(f"t{k}")
+    desc = kernels.chain_descriptor(n_in, body, input_bcast=bc)
+    ins = [_operand(k, R, C, dt, g) * 0.5 for k, dt in zip(bc, dts)]
+    n0 = fpkern.chain_jit_launches()
+    y_jit = fpkern.chain(ins, desc, [R, C], torch.float32)
+    assert fpkern.chain_jit_launches() == n0 + 1
+    y_int = fpkern.chain(ins, desc, [R, C], torch.float32, flags=_lib.FPK_FLAG_NO_JIT)
+    if mode == "flat":
+        assert torch.equal(_bits(y_jit), _bits(y_int))
+    else:
+        _allclose(y_jit, y_int, torch.float32)
