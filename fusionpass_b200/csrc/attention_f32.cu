@@ -6,9 +6,11 @@
 // softmax with f32 running max m_i, sum l_i and accumulator acc, IEEE f32 dot
 // products, out-of-range keys at -inf, one division acc / l_i at the end.
 //
-// 256 threads as a 16 x 16 grid: thread (ty, tx) owns query rows 4*ty..4*ty+3,
-// score columns tx + 16*c and output columns tx + 16*c.  The 16 threads of a
-// row form one half-warp, so the row max / sum are half-warp shuffles.
+// 256 threads as a 16 x 16 grid: thread (ty, tx) owns query rows RPT*ty ..
+// RPT*ty+RPT-1, score columns tx + 16*c and output columns tx + 16*c.  The 16
+// threads of a row form one half-warp, so the row max / sum are half-warp
+// shuffles.  RPT = 4 (64-row query tiles) normally; RPT = 1 (16-row tiles, four
+// times the CTAs) when the 64-row grid would leave most SMs idle.
 #include <atomic>
 #include <cmath>
 
@@ -18,7 +20,6 @@
 namespace fpk {
 namespace attn32 {
 
-constexpr int kBM = 64;
 constexpr int kBN = 64;
 constexpr int kThreads = 256;
 
@@ -32,9 +33,10 @@ struct Params {
   float scale;
 };
 
-template <int D>
+template <int D, int RPT>
 __global__ void __launch_bounds__(kThreads) attn_f32_kernel(const __grid_constant__ Params p) {
   constexpr int DC = D / 16;  // output columns per thread
+  constexpr int kBM = 16 * RPT;  // query rows per CTA
   extern __shared__ __align__(16) float smem_f[];
   float(*Qs)[kBM] = reinterpret_cast<float(*)[kBM]>(smem_f);                          // Qs[d][row]
   float(*Ks)[kBN + 1] = reinterpret_cast<float(*)[kBN + 1]>(smem_f + D * kBM);        // Ks[d][key]
@@ -60,9 +62,9 @@ __global__ void __launch_bounds__(kThreads) attn_f32_kernel(const __grid_constan
     Qs[d][r] = gr < S ? qb[gr * p.qs[2] + d] : 0.0f;
   }
 
-  float m_i[4], l_i[4], acc[4][DC];
+  float m_i[RPT], l_i[RPT], acc[RPT][DC];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < RPT; ++i) {
     m_i[i] = -INFINITY;
     l_i[i] = 0.0f;
 #pragma unroll
@@ -80,27 +82,36 @@ __global__ void __launch_bounds__(kThreads) attn_f32_kernel(const __grid_constan
     }
     __syncthreads();
 
-    float s[4][4];
+    float s[RPT][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < RPT; ++i)
 #pragma unroll
       for (int c = 0; c < 4; ++c) s[i][c] = 0.0f;
 #pragma unroll 8
     for (int d = 0; d < D; ++d) {
-      const float4 qv = *reinterpret_cast<const float4*>(&Qs[d][4 * ty]);
-      const float qa[4] = {qv.x, qv.y, qv.z, qv.w};
+      float qa[RPT];
+      if constexpr (RPT == 4) {
+        const float4 qv = *reinterpret_cast<const float4*>(&Qs[d][4 * ty]);
+        qa[0] = qv.x;
+        qa[1] = qv.y;
+        qa[2] = qv.z;
+        qa[3] = qv.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) qa[i] = Qs[d][RPT * ty + i];
+      }
       float kv[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) kv[c] = Ks[d][tx + 16 * c];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < RPT; ++i)
 #pragma unroll
         for (int c = 0; c < 4; ++c) s[i][c] = fmaf(qa[i], kv[c], s[i][c]);
     }
 
-    float alpha[4];
+    float alpha[RPT];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < RPT; ++i) {
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -116,7 +127,7 @@ __global__ void __launch_bounds__(kThreads) attn_f32_kernel(const __grid_constan
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const float pv = expf(s[i][c] - m_new);
-        Ps[4 * ty + i][tx + 16 * c] = pv;
+        Ps[RPT * ty + i][tx + 16 * c] = pv;
         rs += pv;
       }
 #pragma unroll
@@ -126,56 +137,67 @@ __global__ void __launch_bounds__(kThreads) attn_f32_kernel(const __grid_constan
     }
     __syncthreads();
 
-    float pv_acc[4][DC];
+    float pv_acc[RPT][DC];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < RPT; ++i)
 #pragma unroll
       for (int c = 0; c < DC; ++c) pv_acc[i][c] = 0.0f;
 #pragma unroll 4
     for (int j = 0; j < kBN; ++j) {
-      float pr[4];
+      float pr[RPT];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) pr[i] = Ps[4 * ty + i][j];
+      for (int i = 0; i < RPT; ++i) pr[i] = Ps[RPT * ty + i][j];
 #pragma unroll
       for (int c = 0; c < DC; ++c) {
         const float vv = Vs[j][tx + 16 * c];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) pv_acc[i][c] = fmaf(pr[i], vv, pv_acc[i][c]);
+        for (int i = 0; i < RPT; ++i) pv_acc[i][c] = fmaf(pr[i], vv, pv_acc[i][c]);
       }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < RPT; ++i)
 #pragma unroll
       for (int c = 0; c < DC; ++c) acc[i][c] = acc[i][c] * alpha[i] + pv_acc[i][c];
   }
 
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t gr = m0 + 4 * ty + i;
+  for (int i = 0; i < RPT; ++i) {
+    const int64_t gr = m0 + RPT * ty + i;
     if (gr >= S) continue;
 #pragma unroll
     for (int c = 0; c < DC; ++c) ob[gr * p.os[2] + tx + 16 * c] = acc[i][c] / l_i[i];
   }
 }
 
-template <int D>
+template <int D, int RPT>
 constexpr int smem_bytes() {
+  constexpr int kBM = 16 * RPT;
   return static_cast<int>(sizeof(float)) * (D * kBM + D * (kBN + 1) + kBN * D + kBM * (kBN + 1));
 }
 
-template <int D>
-static int launch_d(const Params& p, int64_t blocks, cudaStream_t s) {
+template <int D, int RPT>
+static int launch_d(Params p, const fpk_attn_desc* d, cudaStream_t s) {
   static std::atomic<int> opted[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FPK_ERR_CUDA;
   if (!opted[dev].load(std::memory_order_acquire)) {
-    if (cudaFuncSetAttribute(attn_f32_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             smem_bytes<D>()) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_f32_kernel<D, RPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem_bytes<D, RPT>()) != cudaSuccess)
       return FPK_ERR_CUDA;
     opted[dev].store(1, std::memory_order_release);
   }
-  attn_f32_kernel<D><<<static_cast<unsigned>(blocks), kThreads, smem_bytes<D>(), s>>>(p);
+  constexpr int kBM = 16 * RPT;
+  p.num_mtiles = (d->seq_len + kBM - 1) / kBM;
+  const int64_t blocks = d->batch * d->heads * p.num_mtiles;
+  if (blocks > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
+  attn_f32_kernel<D, RPT><<<static_cast<unsigned>(blocks), kThreads, smem_bytes<D, RPT>(), s>>>(p);
   return cudaGetLastError() == cudaSuccess ? FPK_OK : FPK_ERR_CUDA;
+}
+
+template <int D>
+static int launch_dd(const Params& p, const fpk_attn_desc* d, int num_sms, cudaStream_t s) {
+  const int64_t blocks64 = d->batch * d->heads * ((d->seq_len + 63) / 64);
+  return blocks64 < num_sms ? launch_d<D, 1>(p, d, s) : launch_d<D, 4>(p, d, s);
 }
 
 }  // namespace attn32
@@ -183,7 +205,6 @@ static int launch_d(const Params& p, int64_t blocks, cudaStream_t s) {
 int launch_attention_f32(const fpk_attn_desc* d, const void* q, const void* k, const void* v, void* o,
                          cudaStream_t stream, const DeviceInfo& dev) {
   using namespace attn32;
-  (void)dev;
   const uintptr_t ptrs[4] = {reinterpret_cast<uintptr_t>(q), reinterpret_cast<uintptr_t>(k),
                              reinterpret_cast<uintptr_t>(v), reinterpret_cast<uintptr_t>(o)};
   for (uintptr_t a : ptrs)
@@ -195,7 +216,7 @@ int launch_attention_f32(const fpk_attn_desc* d, const void* q, const void* k, c
   p.o = static_cast<float*>(o);
   p.heads = d->heads;
   p.seq = d->seq_len;
-  p.num_mtiles = (d->seq_len + kBM - 1) / kBM;
+  p.num_mtiles = 0;  // set by the launch for its tile height
   for (int i = 0; i < 3; ++i) {
     p.qs[i] = d->q_strides[i];
     p.ks[i] = d->k_strides[i];
@@ -203,13 +224,12 @@ int launch_attention_f32(const fpk_attn_desc* d, const void* q, const void* k, c
     p.os[i] = d->o_strides[i];
   }
   p.scale = d->scale;
-  const int64_t blocks = d->batch * d->heads * p.num_mtiles;
-  if (blocks > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
+  const int num_sms = dev.num_sms > 0 ? dev.num_sms : 148;
   switch (d->head_dim) {
-    case 16: return launch_d<16>(p, blocks, stream);
-    case 32: return launch_d<32>(p, blocks, stream);
-    case 64: return launch_d<64>(p, blocks, stream);
-    case 128: return launch_d<128>(p, blocks, stream);
+    case 16: return launch_dd<16>(p, d, num_sms, stream);
+    case 32: return launch_dd<32>(p, d, num_sms, stream);
+    case 64: return launch_dd<64>(p, d, num_sms, stream);
+    case 128: return launch_dd<128>(p, d, num_sms, stream);
     default: return FPK_ERR_UNSUPPORTED;
   }
 }

@@ -220,7 +220,9 @@ def test_attention_f16_unusual_scales(scale):
     _close(out, ref.cpu().numpy(), "f16", f"scale {scale}")
 
 
-@pytest.mark.parametrize("shape", [(1, 2, 300, 64), (2, 1, 77, 128), (1, 3, 65, 16), (1, 1, 1, 32)])
+# small grids run 16-row query tiles, (4, 8, 320, 32) has >= 148 64-row tiles and runs 64-row ones
+@pytest.mark.parametrize("shape", [(1, 2, 300, 64), (2, 1, 77, 128), (1, 3, 65, 16), (1, 1, 1, 32),
+                                   (1, 4, 128, 64), (4, 8, 320, 32)])
 def test_attention_f32_vs_oracle(shape):
     g = torch.Generator().manual_seed(sum(shape) + 1)
     q, k, v = (torch.randn(shape, generator=g) for _ in range(3))
