@@ -1,6 +1,6 @@
 """Generate golden vectors by running the REFERENCE's own kernels on the CPU.
 
-Run once in a container that has the reference checkout (the GPU box does not):
+Run once where the reference checkout is available (the tests only read the fixtures):
 
     TRITON_INTERPRET=1 python tests/golden/make_golden.py [/path/to/reference]
 

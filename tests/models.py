@@ -1,5 +1,5 @@
 """Small torch modules used by the planner and compile tests (same shapes of
-computation as the reference's test modules and the BASELINE workloads)."""
+computation as the reference's test modules and the benchmark workloads)."""
 
 import torch
 import torch.nn.functional as F

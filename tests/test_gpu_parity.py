@@ -1,6 +1,6 @@
 """GPU parity: libfpkern kernels vs the reference's own outputs and the oracle.
 
-Tolerances (from the task's north star, written here on purpose):
+Tolerances against the reference's own kernel outputs (the parity contract):
   f32: |err| <= 1e-5 + 1e-5*|ref|       f16: |err| <= 2e-3 + 1e-2*|ref|
 Chains made only of add/mul/scale/relu are compared bit for bit (the oracle and
 the kernel both do f32 round-to-nearest ops in program order with one final
