@@ -25,7 +25,9 @@
 // attn_tc_kernel, D = 128 (aliased TMEM layout, one CTA per work item): S_t at
 // 128 t, O_t at 256 + 128 t; P_t overwrites the first 64 columns of S_t.  UMMAs
 // issued by one thread execute in order, so Q K^T of the next key tile is
-// issued into S_t right after the P V UMMA that reads P_t from it.
+// issued into S_t right after the P V UMMA that reads P_t from it.  P_t is
+// stored in two halves (keys 0-63, 64-127) with a barrier each: the P V
+// k-steps of the first half run while the softmax still computes the second.
 //
 // In both, the two softmax warpgroups take turns at the exponentials (a pair
 // of turn barriers, handed over before the end of each phase); 2 of every 8
@@ -71,6 +73,9 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;
 constexpr uint32_t kPolyPairs = 0x11u;  // pairs (c/2) mod 8 in {0, 4} use the FMA-pipe exp2
 constexpr int kTurnAt = 104;            // score column after which the exponential turn passes
+constexpr int kHalfSignalAt = 78;       // score column at which the first half of P_t is signalled (D = 128)
+static_assert(kHalfSignalAt % 2 == 0 && kHalfSignalAt >= kBN / 2 - 2 && kHalfSignalAt < kBN,
+              "the half signal follows the store of P for keys 0-63 inside the exponential loop");
 constexpr int kMinSmem = 116 * 1024;  // keeps one CTA per SM (it owns all 512 TMEM columns)
 
 template <int D>
@@ -103,6 +108,7 @@ struct Bars {
   uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
   // p_full / turn: one arrival per softmax warp (lane 0 after __syncwarp)
   uint64_t s_full[kTiles], p_full[kTiles], o_done[kTiles];
+  uint64_t p_half[kTiles];  // P_t of keys 0-63 is in TMEM
   uint64_t turn[kTiles];    // ping-pong of the exponential phases of the two tiles
   uint64_t epi[kTiles];     // the 4 warps of a tile before the O store (a bounded wait)
   uint64_t drain;
@@ -419,6 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < kTiles; ++t) {
       mbar_init(&bars.s_full[t], 1);
+      mbar_init(&bars.p_half[t], kWG / 32);
       mbar_init(&bars.p_full[t], kWG / 32);
       mbar_init(&bars.o_done[t], 1);
       mbar_init(&bars.turn[t], kWG / 32);
@@ -502,14 +509,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_ss_l(leader, d_tmem, a0 + off, b0 + off, idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](int t, int s, bool accumulate) {
+      // P V k-steps of one half of the keys (half 0: keys 0-63, half 1: 64-127)
+      auto issue_pv = [&](int t, int s, bool accumulate, int half) {
         const uint32_t d_tmem = tbase + kOCol0 + static_cast<uint32_t>(t) * kOStride;
         const uint32_t a_tmem = tbase + kPCol0 + static_cast<uint32_t>(t) * kPStride;
         const uint64_t b0 = v_desc + static_cast<uint64_t>(s) * kTileStep;
   #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
+        for (int k2 = 0; k2 < kBN / 32; ++k2) {
+          const int kk = half * (kBN / 32) + k2;
           mma_ts_l(leader, d_tmem, a_tmem + static_cast<uint32_t>(kk * 8),
                    b0 + static_cast<uint64_t>(kk * C::kRowBytes), idesc_pv, (accumulate || kk > 0) ? 1u : 0u);
+        }
       };
       bool ok = mbar_wait_w(&bars.q_full, 0, abort, p.status, limit) &&
                 mbar_wait_w(&bars.k_full[0], 0, abort, p.status, limit);
@@ -527,12 +537,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool more = j + 1 < nkv;
         if (!mbar_wait_w(&bars.v_full[s], r, abort, p.status, limit)) break;
         for (int t = 0; t < ntiles; ++t) {
+          if (!mbar_wait_w(&bars.p_half[t], static_cast<uint32_t>(j) & 1u, abort, p.status, limit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(t, s, j > 0, 0);
           if (!mbar_wait_w(&bars.p_full[t], static_cast<uint32_t>(j) & 1u, abort, p.status, limit)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv(t, s, j > 0);
+          issue_pv(t, s, j > 0, 1);
           mma_commit_l(leader, &bars.o_done[t]);
           if (more) {
             if (t == 0 && !mbar_wait_w(&bars.k_full[s1], r1, abort, p.status, limit)) {
@@ -642,7 +658,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // p = 2^(s * scale * log2 e - m); P packed to f16 pairs in place (sr[c/2])
         // 2 of every 8 pairs take the FMA-pipe exp2, the rest the MUFU; the turn
         // passes to the other tile a quarter before the end, so its wake-up
-        // overlaps this tile's last exponentials.
+        // overlaps this tile's last exponentials.  P of keys 0-63 goes to TMEM
+        // once computed and is signalled a few pairs later (its store has
+        // landed by then), so its P V k-steps start during the second half.
 #pragma unroll
         for (int c = 0; c < kBN; c += 2) {
           float x0, x1, p0, p1;
@@ -655,13 +673,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           add2(la[(c >> 1) & 3], lb[(c >> 1) & 3], p0, p1);
           sr[c >> 1] = pack_half2(p0, p1);
+          if (c == kBN / 2 - 2) tmem_st_x32(tP, sr);
+          if (c == kHalfSignalAt) {
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.p_half[t]);
+          }
           if (c == kTurnAt && ntiles == 2) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars.turn[1 - t]);
           }
         }
         l += ((la[0] + lb[0]) + (la[1] + lb[1])) + ((la[2] + lb[2]) + (la[3] + lb[3]));
-        tmem_st_x64(tP, sr);
+        tmem_st_x32(tP + 32u, sr + 32);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
