@@ -301,7 +301,10 @@ def run_configs(args, group: "RankGroup", rank: int, world: int, dev) -> dict:
             "launches": reps, "ms_per_launch": round(ms / reps, 3),
             "value": round(weak_rate(world, reps, flop, ms) / 1e12, 2), "unit": "TFLOP/s",
             "roofline_frac": round(tf / pk4["tc"], 4),
-            "roofline_frac_of_sustained": round(tf / pk4["tc_sustained"], 4)}
+            "roofline_frac_of_sustained": round(tf / pk4["tc_sustained"], 4),
+            # Q, K, V read once and O written once: 4 * 268 MB per launch
+            "algorithmic_bytes_per_launch": 4 * 4 * 32 * 8192 * 128 * 2,
+            "traffic": ncu_traffic().get("attention_long", {}).get("dram_bytes_per_launch")}
         del q4, k4, v4, o4
 
     # cfg5: BERT-base block, batch 32 seq 512 hidden 768 heads 12 FFN 3072, f16
