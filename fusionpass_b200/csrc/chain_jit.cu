@@ -6,10 +6,12 @@
 // launch.  This is the sm_100a counterpart for flat chains: the descriptor's op
 // list becomes straight-line f32 CUDA (one SSA value per op), NVRTC compiles it
 // for sm_100a on first use, and the cubin is loaded with cudaLibraryLoadData and
-// cached by source text for the life of the process.  The interpreter kernels
-// in chain.cu stay the path for every case this tier does not take (rows mode,
-// ragged column counts, unaligned pointers, no run-time compiler, a stream
-// under capture before the first compile, the device-wait test flag).
+// cached by source text for the life of the process.  Rows chains (one
+// last-axis softmax, up to 16384 columns) get a generated kernel of their own
+// (gen_rows_source).  The interpreter kernels in chain.cu stay the path for every
+// case this tier does not take (ragged column counts, longer rows, unaligned
+// pointers, no run-time compiler, a stream under capture before the first
+// compile, the device-wait test flag).
 //
 // Generated kernel: each thread owns 8 consecutive elements of a row (one
 // 16-byte vector of f16, two of f32) per step and walks the flattened
@@ -19,7 +21,7 @@
 // Full-shape operands are read and the result written with streaming
 // (evict-first) cache hints.  Arithmetic uses the same op definitions as the
 // interpreter (chain_ops.cuh, embedded below) with explicit round-to-nearest
-// adds and multiplies, so both tiers are bit-identical.
+// adds and multiplies, so both tiers are bit-identical for flat chains.
 #include <dlfcn.h>
 #include <nvrtc.h>
 
@@ -157,6 +159,8 @@ __device__ __forceinline__ void unpack8(uint4 u, float* a) {
   a[4] = h2f((u16)(u.z & 0xffffu)); a[5] = h2f((u16)(u.z >> 16));
   a[6] = h2f((u16)(u.w & 0xffffu)); a[7] = h2f((u16)(u.w >> 16));
 }
+// 2^x on the MUFU, subnormal results kept (rows softmax)
+__device__ __forceinline__ float ex2f_approx(float x) { float y; asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x)); return y; }
 // full-shape operands: streaming loads (read once, evict first)
 __device__ __forceinline__ void ld8s_f16(const void* b, i64 off, float* a) {
   unpack8(__ldcs(reinterpret_cast<const uint4*>(reinterpret_cast<const u16*>(b) + off)), a);
@@ -287,9 +291,13 @@ static std::string gen_flat_source(const fpk_chain_desc* d) {
 // constant, so a row's values stay in registers: TPR threads share a row, each
 // loads its VPT vectors, evaluates the ops before the softmax, reduces the row
 // max and sum (shuffles within a warp, shared memory across the warps of a row),
-// then evaluates the ops after it and stores.  Softmax arithmetic as the
-// interpreter's: e = exp(x - max) (0 for masked columns), sum by round-to-nearest
-// adds, p = e / sum.
+// then evaluates the ops after it and stores.  Softmax: e = 2^((x - max) * log2 e)
+// on the MUFU (ex2.approx, relative error ~5e-7 for every e that is not
+// negligible against the row sum; 0 for masked columns), sum by round-to-nearest
+// adds, p = e * (1 / sum) with a correctly rounded reciprocal.  An accurate expf
+// and an IEEE division per element made this kernel instruction-bound (~40
+// instructions per element); these are ~5 and it is bandwidth-bound.  Results
+// agree with the interpreter (expf, e / sum) within 2e-5 relative for f32.
 static std::string gen_rows_source(const fpk_chain_desc* d) {
   const int nin = d->n_inputs;
   const RowsGeom g = rows_geom(d->cols);
@@ -362,14 +370,16 @@ static std::string gen_rows_source(const fpk_chain_desc* d) {
   }
   app(s, "  float ev[E];\n  float sum = 0.0f;\n  #pragma unroll\n  for (int e = 0; e < E; ++e) {\n"
          "    const float x = %s ? v%d[e] : -INFINITY;\n"
-         "    ev[e] = (x == -INFINITY) ? 0.0f : expf(__fsub_rn(x, m));\n    sum = __fadd_rn(sum, ev[e]);\n  }\n",
+         "    ev[e] = (x == -INFINITY) ? 0.0f : ex2f_approx(__fmul_rn(__fsub_rn(x, m), 1.44269504088896341f));\n"
+         "    sum = __fadd_rn(sum, ev[e]);\n  }\n",
       valid, src);
   app(s, "  #pragma unroll\n  for (int off = (TPR < 32 ? TPR : 32) / 2; off > 0; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));\n");
   if (wpr > 1) {
     s += "  if ((threadIdx.x & 31) == 0) red[1][rl][t >> 5] = sum;\n  __syncthreads();\n";
     s += "  sum = red[1][rl][0];\n  #pragma unroll\n  for (int w = 1; w < WPR; ++w) sum = __fadd_rn(sum, red[1][rl][w]);\n";
   }
-  app(s, "  float v%d[E];\n  #pragma unroll\n  for (int e = 0; e < E; ++e) v%d[e] = __fdiv_rn(ev[e], sum);\n", dst, dst);
+  // 0 * (1 / 0) is NaN like 0 / 0 for a row whose every value is masked
+  app(s, "  const float rsum = __frcp_rn(sum);\n  float v%d[E];\n  #pragma unroll\n  for (int e = 0; e < E; ++e) v%d[e] = __fmul_rn(ev[e], rsum);\n", dst, dst);
   for (int k = ksm + 1; k < d->n_ops; ++k) emit_op(k);
   app(s, "  if (live) {\n  #pragma unroll\n  for (int k = 0; k < VPT; ++k) {\n    const int vv = k * TPR + t;\n"
          "    if (vv < NV) st8_%s(p.out, base + vv * 8, v%d + k * 8);\n  }\n  }\n}\n",
