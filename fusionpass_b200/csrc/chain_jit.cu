@@ -13,13 +13,14 @@
 // pointers, no run-time compiler, a stream under capture before the first
 // compile, the device-wait test flag).
 //
-// Generated kernel: each thread owns 8 consecutive elements of a row (one
-// 16-byte vector of f16, two of f32) per step and walks the flattened
-// [rows, cols/8] vector grid with a grid stride; column operands are reloaded
-// only when the thread's column changes, row operands when its row changes.
-// Two vectors are loaded before either is computed, for memory parallelism.
-// Full-shape operands are read and the result written with streaming
-// (evict-first) cache hints.  Arithmetic uses the same op definitions as the
+// Generated flat kernel: the flattened [rows, cols/8] grid of 8-element vectors
+// (16 bytes of f16, 32 of f32) is cut into consecutive runs of 128 vectors, one
+// per 64-thread CTA, which makes a single pass: thread t takes vectors t and
+// t + 64 of its run (each load instruction of a warp covers 512 contiguous
+// bytes), loads both before computing either, and stores both.  Per-column and
+// per-row operands are read per vector through the read-only cache (they stay
+// in L1/L2).  Full-shape operands are read and the result written with
+// streaming (evict-first) cache hints.  Arithmetic uses the same op definitions as the
 // interpreter (chain_ops.cuh, embedded below) with explicit round-to-nearest
 // adds and multiplies, so both tiers are bit-identical for flat chains.
 #include <dlfcn.h>
@@ -46,11 +47,13 @@ static const char kOpsSrc[] =
     ;
 
 constexpr int kVec = 8;        // elements per thread-vector
-// 64-thread CTAs, 16 per SM (1024 threads per SM, each with two 16-byte vectors
-// per full operand in flight): the fastest of the shapes measured on B200 for a
-// 4096 x 4096 f16 chain (13.6 us vs 14.7 us for 256 x 8 and 16 us for 1024 x 2).
-constexpr int kBlock = 64;      // threads per CTA of the generated kernel
-constexpr int kCtasPerSm = 16;  // CTAs per SM in the grid-stride launch
+// One pass per 64-thread CTA with two vectors per thread: the fastest of the
+// shapes measured on B200 for a 4096 x 4096 f16 chain (12.6 us; 12.7-13.0 us for
+// 96 or 128 threads or three vectors, 13.7-18 us for 512 threads, one vector per
+// 64 threads or four; 13.3 us for the earlier persistent grid-stride kernel of
+// 16 CTAs per SM).
+constexpr int kBlock = 64;         // threads per CTA of the generated flat kernel
+constexpr int kVecsPerThread = 2;  // vectors per thread (one pass)
 
 struct JitParams {
   const void* in[FPK_CHAIN_MAX_INPUTS];
@@ -200,96 +203,70 @@ __device__ __forceinline__ void st8_f32(void* b, i64 off, const float* y) {
 )SRC";
 }
 
+// Flat chains: one pass per CTA over kBlock * kVecsPerThread consecutive vectors
+// (vector w of the run at thread w % kBlock), all full-shape loads first.
 static std::string gen_flat_source(const fpk_chain_desc* d) {
   const int nin = d->n_inputs;
+  const int U = kVecsPerThread;
   std::string s;
   prelude(s);
   const char* dt[2] = {"f32", "f16"};
   auto idt = [&](int i) { return dt[d->in_dtype[i] == FPK_F16 ? 1 : 0]; };
-
   app(s, "extern \"C\" __global__ void __launch_bounds__(%d) fpk_jit_chain(const JitParams p) {\n", kBlock);
-  s += "  const i64 stride = (i64)gridDim.x * blockDim.x;\n";
-  s += "  i64 v = (i64)blockIdx.x * blockDim.x + threadIdx.x;\n";
-  s += "  if (v >= p.nvec) return;\n";
-  s += "  const i64 drow = stride / p.ncv, dcv = stride - drow * p.ncv;\n";
-  s += "  i64 row0 = v / p.ncv, cv0 = v - row0 * p.ncv;\n";
-  // broadcast operand state
-  for (int i = 0; i < nin; ++i) {
-    switch (d->in_bcast[i]) {
-      case FPK_BCAST_COL:
-        app(s, "  float c%d[8]; i64 c%d_at = -1;\n", i, i);
-        break;
-      case FPK_BCAST_ROW:
-        app(s, "  float r%d = 0.0f; i64 r%d_at = -1;\n", i, i);
-        break;
-      case FPK_BCAST_SCALAR:
-        app(s, "  const float s%d = ld1_%s(p.in[%d], 0);\n", i, idt(i), i);
-        break;
-      default:
-        break;
-    }
+  app(s, "  const i64 v0 = (i64)blockIdx.x * (%d * %d) + threadIdx.x;\n", kBlock, U);
+  for (int i = 0; i < nin; ++i)
+    if (d->in_bcast[i] == FPK_BCAST_SCALAR) app(s, "  const float s%d = ld1_%s(p.in[%d], 0);\n", i, idt(i), i);
+  for (int u = 0; u < U; ++u) {
+    app(s, "  const i64 w%d = v0 + %d;\n  const bool h%d = w%d < p.nvec;\n", u, u * kBlock, u, u);
+    app(s, "  const i64 off%d = w%d * 8;\n", u, u);
   }
-  s += "  for (; v < p.nvec; v += 2 * stride) {\n";
-  s += "    const bool two = v + stride < p.nvec;\n";
-  s += "    i64 row1 = row0 + drow, cv1 = cv0 + dcv;\n";
-  s += "    if (cv1 >= p.ncv) { cv1 -= p.ncv; ++row1; }\n";
-  s += "    const i64 off0 = v * 8, off1 = (v + stride) * 8;  // element offsets (cols % 8 == 0)\n";
-  // full-shape loads for both vectors first
   for (int i = 0; i < nin; ++i) {
     if (d->in_bcast[i] != FPK_BCAST_FULL) continue;
-    app(s, "    float a%d_0[8], a%d_1[8];\n", i, i);
-    app(s, "    ld8s_%s(p.in[%d], off0, a%d_0);\n", idt(i), i, i);
-    app(s, "    if (two) ld8s_%s(p.in[%d], off1, a%d_1);\n", idt(i), i, i);
-  }
-  for (int u = 0; u < 2; ++u) {
-    if (u == 1) s += "    if (two) {\n";
-    const char* ind = u == 1 ? "      " : "    ";
-    app(s, "%s{\n", ind);
-    for (int i = 0; i < nin; ++i) {
-      if (d->in_bcast[i] == FPK_BCAST_COL)
-        app(s, "%s  if (cv%d != c%d_at) { ld8c_%s(p.in[%d], cv%d * 8, c%d); c%d_at = cv%d; }\n", ind, u, i, idt(i), i,
-            u, i, i, u);
-      else if (d->in_bcast[i] == FPK_BCAST_ROW)
-        app(s, "%s  if (row%d != r%d_at) { r%d = ld1_%s(p.in[%d], row%d); r%d_at = row%d; }\n", ind, u, i, i,
-            idt(i), i, u, i, u);
+    for (int u = 0; u < U; ++u) {
+      app(s, "  float a%d_%d[8];\n", i, u);
+      app(s, "  if (h%d) ld8s_%s(p.in[%d], off%d, a%d_%d);\n", u, idt(i), i, u, i, u);
     }
-    app(s, "%s  float y[8];\n", ind);
-    app(s, "%s  #pragma unroll\n", ind);
-    app(s, "%s  for (int e = 0; e < 8; ++e) {\n", ind);
+  }
+  for (int u = 0; u < U; ++u) {
+    app(s, "  if (h%d) {\n", u);
+    const char* ind = "    ";
+    bool need_pos = false;
+    for (int i = 0; i < nin; ++i) need_pos |= d->in_bcast[i] == FPK_BCAST_COL || d->in_bcast[i] == FPK_BCAST_ROW;
+    if (need_pos) app(s, "%sconst i64 row = w%d / p.ncv, cv = w%d - row * p.ncv;\n", ind, u, u);
+    for (int i = 0; i < nin; ++i) {
+      if (d->in_bcast[i] == FPK_BCAST_COL) app(s, "%sfloat c%d[8]; ld8c_%s(p.in[%d], cv * 8, c%d);\n", ind, i, idt(i), i, i);
+      else if (d->in_bcast[i] == FPK_BCAST_ROW) app(s, "%sconst float r%d = ld1_%s(p.in[%d], row);\n", ind, i, idt(i), i);
+    }
+    app(s, "%sfloat y[8];\n%s#pragma unroll\n%sfor (int e = 0; e < 8; ++e) {\n", ind, ind, ind);
     for (int i = 0; i < nin; ++i) {
       switch (d->in_bcast[i]) {
-        case FPK_BCAST_FULL: app(s, "%s    const float v%d = a%d_%d[e];\n", ind, i, i, u); break;
-        case FPK_BCAST_COL: app(s, "%s    const float v%d = c%d[e];\n", ind, i, i); break;
-        case FPK_BCAST_ROW: app(s, "%s    const float v%d = r%d;\n", ind, i, i); break;
-        default: app(s, "%s    const float v%d = s%d;\n", ind, i, i); break;
+        case FPK_BCAST_FULL: app(s, "%s  const float v%d = a%d_%d[e];\n", ind, i, i, u); break;
+        case FPK_BCAST_COL: app(s, "%s  const float v%d = c%d[e];\n", ind, i, i); break;
+        case FPK_BCAST_ROW: app(s, "%s  const float v%d = r%d;\n", ind, i, i); break;
+        default: app(s, "%s  const float v%d = s%d;\n", ind, i, i); break;
       }
     }
     for (int k = 0; k < d->n_ops; ++k) {
       const fpk_chain_op& op = d->ops[k];
       const int dst = nin + k;
       switch (op.opcode) {
-        case FPK_OP_ADD: app(s, "%s    const float v%d = __fadd_rn(v%d, v%d);\n", ind, dst, op.src_a, op.src_b); break;
-        case FPK_OP_MUL: app(s, "%s    const float v%d = __fmul_rn(v%d, v%d);\n", ind, dst, op.src_a, op.src_b); break;
+        case FPK_OP_ADD: app(s, "%s  const float v%d = __fadd_rn(v%d, v%d);\n", ind, dst, op.src_a, op.src_b); break;
+        case FPK_OP_MUL: app(s, "%s  const float v%d = __fmul_rn(v%d, v%d);\n", ind, dst, op.src_a, op.src_b); break;
         case FPK_OP_SCALE: {
           uint32_t bits;
           std::memcpy(&bits, &op.imm, 4);
-          app(s, "%s    const float v%d = __fmul_rn(v%d, __uint_as_float(0x%08xu));\n", ind, dst, op.src_a, bits);
+          app(s, "%s  const float v%d = __fmul_rn(v%d, __uint_as_float(0x%08xu));\n", ind, dst, op.src_a, bits);
           break;
         }
-        case FPK_OP_RELU: app(s, "%s    const float v%d = op_relu(v%d);\n", ind, dst, op.src_a); break;
-        case FPK_OP_EXP: app(s, "%s    const float v%d = expf(v%d);\n", ind, dst, op.src_a); break;
-        default: app(s, "%s    const float v%d = op_gelu(v%d);\n", ind, dst, op.src_a); break;
+        case FPK_OP_RELU: app(s, "%s  const float v%d = op_relu(v%d);\n", ind, dst, op.src_a); break;
+        case FPK_OP_EXP: app(s, "%s  const float v%d = expf(v%d);\n", ind, dst, op.src_a); break;
+        default: app(s, "%s  const float v%d = op_gelu(v%d);\n", ind, dst, op.src_a); break;
       }
     }
-    app(s, "%s    y[e] = v%d;\n", ind, d->result);
-    app(s, "%s  }\n", ind);
-    app(s, "%s  st8_%s(p.out, off%d, y);\n", ind, d->out_dtype == FPK_F16 ? "f16" : "f32", u);
-    app(s, "%s}\n", ind);
-    if (u == 1) s += "    }\n";
+    app(s, "%s  y[e] = v%d;\n%s}\n", ind, d->result, ind);
+    app(s, "%sst8_%s(p.out, off%d, y);\n  }\n", ind, d->out_dtype == FPK_F16 ? "f16" : "f32", u);
   }
-  s += "    row0 = row1 + drow; cv0 = cv1 + dcv;\n";
-  s += "    if (cv0 >= p.ncv) { cv0 -= p.ncv; ++row0; }\n";
-  s += "  }\n}\n";
+  s += "}\n";
   return s;
 }
 
@@ -366,19 +343,25 @@ static std::string gen_rows_source(const fpk_chain_desc* d) {
   for (int k = 0; k < ksm; ++k) emit_op(k);
   // the softmax
   const int src = d->ops[ksm].src_a, dst = nin + ksm;
-  auto valid = "(((e >> 3) * TPR + t) < NV)";
-  app(s, "  float m = -INFINITY;\n  #pragma unroll\n  for (int e = 0; e < E; ++e) if (%s) m = fmaxf(m, v%d[e]);\n",
-      valid, src);
+  // slots past the row end exist only when VPT * TPR > NV (ragged rows)
+  const bool pad = g.vpt * g.tpr > g.nv;
+  const char* xval = pad ? "((((e >> 3) * TPR + t) < NV) ? v%d[e] : -INFINITY)" : "v%d[e]";
+  char xexpr[128];
+  std::snprintf(xexpr, sizeof(xexpr), xval, src);
+  // row max in four independent chains
+  app(s, "  float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};\n  #pragma unroll\n"
+         "  for (int e = 0; e < E; ++e) mq[e & 3] = fmaxf(mq[e & 3], %s);\n"
+         "  float m = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));\n", xexpr);
   app(s, "  #pragma unroll\n  for (int off = (TPR < 32 ? TPR : 32) / 2; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));\n");
   if (wpr > 1) {
     s += "  if ((threadIdx.x & 31) == 0) red[0][rl][t >> 5] = m;\n  __syncthreads();\n";
     s += "  m = red[0][rl][0];\n  #pragma unroll\n  for (int w = 1; w < WPR; ++w) m = fmaxf(m, red[0][rl][w]);\n";
   }
-  app(s, "  float ev[E];\n  float sum = 0.0f;\n  #pragma unroll\n  for (int e = 0; e < E; ++e) {\n"
-         "    const float x = %s ? v%d[e] : -INFINITY;\n"
-         "    ev[e] = (x == -INFINITY) ? 0.0f : ex2f_approx(__fmul_rn(__fsub_rn(x, m), 1.44269504088896341f));\n"
-         "    sum = __fadd_rn(sum, ev[e]);\n  }\n",
-      valid, src);
+  // e = 2^((x - m) log2 e): a -inf score (or a slot past the row end) gives 0 for any finite m
+  app(s, "  float ev[E];\n  float sq[4] = {0.0f, 0.0f, 0.0f, 0.0f};\n  #pragma unroll\n  for (int e = 0; e < E; ++e) {\n"
+         "    ev[e] = ex2f_approx(__fmul_rn(__fsub_rn(%s, m), 1.44269504088896341f));\n"
+         "    sq[e & 3] = __fadd_rn(sq[e & 3], ev[e]);\n  }\n"
+         "  float sum = __fadd_rn(__fadd_rn(sq[0], sq[1]), __fadd_rn(sq[2], sq[3]));\n", xexpr);
   app(s, "  #pragma unroll\n  for (int off = (TPR < 32 ? TPR : 32) / 2; off > 0; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));\n");
   if (wpr > 1) {
     s += "  if ((threadIdx.x & 31) == 0) red[1][rl][t >> 5] = sum;\n  __syncthreads();\n";
@@ -513,10 +496,9 @@ int try_launch_chain_jit(const fpk_chain_desc* d, const void* const* inputs, voi
     block = g.block;
     if (grid > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
   } else {
-    const long long per_cta = static_cast<long long>(kBlock) * 2;  // two vectors per thread and step
+    const long long per_cta = static_cast<long long>(kBlock) * kVecsPerThread;  // one pass per CTA
     grid = (p.nvec + per_cta - 1) / per_cta;
-    const long long cap = static_cast<long long>(dev.num_sms > 0 ? dev.num_sms : 148) * kCtasPerSm;
-    if (grid > cap) grid = cap;
+    if (grid > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
     block = kBlock;
   }
   void* args[] = {&p};
