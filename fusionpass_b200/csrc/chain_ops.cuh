@@ -13,9 +13,33 @@ __device__ __forceinline__ float op_relu(float x) {
   return y;
 }
 
-// 0.5 x (1 + erf(x / sqrt 2)), each step rounded as written
+// 0.5 x (1 + erf(x / sqrt 2)).  With t = x / sqrt 2 and z = |t|, 1 + erf(t) is
+// erfc(z) for t < 0 and 2 - erfc(z) otherwise; erfc(z) = u exp(-z^2 + P(u)) with
+// u = 1 / (1 + z / 2) and P the degree-9 Chebyshev fit of Numerical Recipes'
+// erfcc (fractional error below 1.2e-7 for every z >= 0).  One reciprocal and one
+// exp2 on the MUFU and eleven FMAs: 48 vs 59 us for bias + GELU over f16 [16384, 3072]
+// with erff, which made the chain instruction-bound.  Against 0.5 x (1 + erf) in
+// double precision: max abs error 3.8e-7 (erff form 4.5e-7), max relative error
+// 2.9e-6 for |x| < 5, where the erff form lost up to 5e-2 to the cancellation in
+// 1 + erf(t) for negative t.
 __device__ __forceinline__ float op_gelu(float x) {
   const float t = __fmul_rn(x, 0.70710678118654752f);
-  const float e = erff(t);
-  return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.0f, e));
+  const float z = fabsf(t);
+  float u;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(u) : "f"(fmaf(0.5f, z, 1.0f)));
+  float p = 0.17087277f;
+  p = fmaf(p, u, -0.82215223f);
+  p = fmaf(p, u, 1.48851587f);
+  p = fmaf(p, u, -1.13520398f);
+  p = fmaf(p, u, 0.27886807f);
+  p = fmaf(p, u, -0.18628806f);
+  p = fmaf(p, u, 0.09678418f);
+  p = fmaf(p, u, 0.37409196f);
+  p = fmaf(p, u, 1.00002368f);
+  p = fmaf(p, u, -1.26551223f);
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(__fmul_rn(fmaf(-z, z, p), 1.44269504088896341f)));
+  const float erfc_z = __fmul_rn(u, e);
+  const float one_plus_erf = t < 0.0f ? erfc_z : __fsub_rn(2.0f, erfc_z);
+  return __fmul_rn(__fmul_rn(x, 0.5f), one_plus_erf);
 }
