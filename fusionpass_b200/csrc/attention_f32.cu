@@ -10,7 +10,11 @@
 // RPT*ty+RPT-1, score columns tx + 16*c and output columns tx + 16*c.  The 16
 // threads of a row form one half-warp, so the row max / sum are half-warp
 // shuffles.  RPT = 4 (64-row query tiles) normally; RPT = 1 (16-row tiles, four
-// times the CTAs) when the 64-row grid would leave most SMs idle.
+// times the CTAs) when the 64-row grid would leave most SMs idle.  With 16-row
+// tiles a CTA may also split its key tiles over G groups of 256 threads (key tile
+// j to group j % G, each group with its own K / V / P buffers and its own named
+// barrier); the groups' (m, l, acc) are merged through shared memory at the end:
+// m = max m_g, l = sum l_g e^(m_g - m), acc = sum acc_g e^(m_g - m).
 #include <atomic>
 #include <cmath>
 
@@ -33,17 +37,36 @@ struct Params {
   float scale;
 };
 
+// floats of one group's K / V / P buffers
 template <int D, int RPT>
-__global__ void __launch_bounds__(kThreads) attn_f32_kernel(const __grid_constant__ Params p) {
+__host__ __device__ constexpr int group_floats() {
+  return D * (kBN + 1) + kBN * D + 16 * RPT * (kBN + 1);
+}
+
+// threads of group `grp` only (named barrier 1 + grp; barrier 0 is __syncthreads)
+template <int G>
+__device__ __forceinline__ void group_sync(int grp) {
+  if constexpr (G == 1) {
+    __syncthreads();
+  } else {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(kThreads) : "memory");
+  }
+}
+
+template <int D, int RPT, int G>
+__global__ void __launch_bounds__(kThreads * G) attn_f32_kernel(const __grid_constant__ Params p) {
+  static_assert(G == 1 || RPT == 1, "key groups are used with 16-row tiles");
   constexpr int DC = D / 16;  // output columns per thread
   constexpr int kBM = 16 * RPT;  // query rows per CTA
   extern __shared__ __align__(16) float smem_f[];
-  float(*Qs)[kBM] = reinterpret_cast<float(*)[kBM]>(smem_f);                          // Qs[d][row]
-  float(*Ks)[kBN + 1] = reinterpret_cast<float(*)[kBN + 1]>(smem_f + D * kBM);        // Ks[d][key]
-  float(*Vs)[D] = reinterpret_cast<float(*)[D]>(smem_f + D * kBM + D * (kBN + 1));   // Vs[key][d]
-  float(*Ps)[kBN + 1] = reinterpret_cast<float(*)[kBN + 1]>(smem_f + D * kBM + D * (kBN + 1) + kBN * D);
+  const int grp = G == 1 ? 0 : static_cast<int>(threadIdx.x) / kThreads;
+  float* gbuf = smem_f + D * kBM + grp * group_floats<D, RPT>();
+  float(*Qs)[kBM] = reinterpret_cast<float(*)[kBM]>(smem_f);                      // Qs[d][row]
+  float(*Ks)[kBN + 1] = reinterpret_cast<float(*)[kBN + 1]>(gbuf);                // Ks[d][key]
+  float(*Vs)[D] = reinterpret_cast<float(*)[D]>(gbuf + D * (kBN + 1));           // Vs[key][d]
+  float(*Ps)[kBN + 1] = reinterpret_cast<float(*)[kBN + 1]>(gbuf + D * (kBN + 1) + kBN * D);
 
-  const int tid = threadIdx.x;
+  const int tid = static_cast<int>(threadIdx.x) % kThreads;  // thread within its group
   const int tx = tid & 15;
   const int ty = tid >> 4;
   const int64_t bh = blockIdx.x / p.num_mtiles;
@@ -56,7 +79,7 @@ __global__ void __launch_bounds__(kThreads) attn_f32_kernel(const __grid_constan
   const int64_t S = p.seq;
 
   // Q tile -> Qs (rows past S read as 0, kernels.py:66-67)
-  for (int idx = tid; idx < kBM * D; idx += kThreads) {
+  for (int idx = static_cast<int>(threadIdx.x); idx < kBM * D; idx += kThreads * G) {
     const int r = idx % kBM, d = idx / kBM;
     const int64_t gr = m0 + r;
     Qs[d][r] = gr < S ? qb[gr * p.qs[2] + d] : 0.0f;
@@ -71,8 +94,9 @@ __global__ void __launch_bounds__(kThreads) attn_f32_kernel(const __grid_constan
     for (int c = 0; c < DC; ++c) acc[i][c] = 0.0f;
   }
 
-  for (int64_t n0 = 0; n0 < S; n0 += kBN) {
-    __syncthreads();  // previous tile fully consumed (and Qs written on the first pass)
+  if constexpr (G > 1) __syncthreads();  // Qs written by every group
+  for (int64_t n0 = static_cast<int64_t>(grp) * kBN; n0 < S; n0 += static_cast<int64_t>(G) * kBN) {
+    group_sync<G>(grp);  // previous tile fully consumed (and Qs written on the first pass)
     for (int idx = tid; idx < kBN * D; idx += kThreads) {
       const int j = idx / D, d = idx % D;
       const int64_t gj = n0 + j;
@@ -80,7 +104,7 @@ __global__ void __launch_bounds__(kThreads) attn_f32_kernel(const __grid_constan
       Ks[d][j] = ok ? kb[gj * p.ks[2] + d] : 0.0f;
       Vs[j][d] = ok ? vb[gj * p.vs[2] + d] : 0.0f;
     }
-    __syncthreads();
+    group_sync<G>(grp);
 
     float s[RPT][4];
 #pragma unroll
@@ -135,7 +159,7 @@ __global__ void __launch_bounds__(kThreads) attn_f32_kernel(const __grid_constan
       l_i[i] = l_i[i] * alpha[i] + rs;
       m_i[i] = m_new;
     }
-    __syncthreads();
+    group_sync<G>(grp);
 
     float pv_acc[RPT][DC];
 #pragma unroll
@@ -160,6 +184,38 @@ __global__ void __launch_bounds__(kThreads) attn_f32_kernel(const __grid_constan
       for (int c = 0; c < DC; ++c) acc[i][c] = acc[i][c] * alpha[i] + pv_acc[i][c];
   }
 
+  if constexpr (G > 1) {
+    // merge the groups: each group's (m, l, acc) of its rows into its own K buffer
+    __syncthreads();
+    {
+      float* r = gbuf + ty * (D + 2);  // [kBM][D + 2]: acc, then m and l
+#pragma unroll
+      for (int c = 0; c < DC; ++c) r[tx + 16 * c] = acc[0][c];
+      if (tx == 0) {
+        r[D] = m_i[0];
+        r[D + 1] = l_i[0];
+      }
+    }
+    __syncthreads();
+    if (grp != 0) return;
+    float m = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < G; ++q) m = fmaxf(m, smem_f[D * kBM + q * group_floats<D, RPT>() + ty * (D + 2) + D]);
+    float l = 0.0f, a[DC];
+#pragma unroll
+    for (int c = 0; c < DC; ++c) a[c] = 0.0f;
+#pragma unroll
+    for (int q = 0; q < G; ++q) {
+      const float* r = smem_f + D * kBM + q * group_floats<D, RPT>() + ty * (D + 2);
+      const float w = r[D] == -INFINITY ? 0.0f : expf(r[D] - m);  // a group without keys adds nothing
+      l += r[D + 1] * w;
+#pragma unroll
+      for (int c = 0; c < DC; ++c) a[c] += r[tx + 16 * c] * w;
+    }
+    l_i[0] = l;
+#pragma unroll
+    for (int c = 0; c < DC; ++c) acc[0][c] = a[c];
+  }
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
     const int64_t gr = m0 + RPT * ty + i;
@@ -169,20 +225,21 @@ __global__ void __launch_bounds__(kThreads) attn_f32_kernel(const __grid_constan
   }
 }
 
-template <int D, int RPT>
+template <int D, int RPT, int G>
 constexpr int smem_bytes() {
   constexpr int kBM = 16 * RPT;
-  return static_cast<int>(sizeof(float)) * (D * kBM + D * (kBN + 1) + kBN * D + kBM * (kBN + 1));
+  return static_cast<int>(sizeof(float)) * (D * kBM + G * group_floats<D, RPT>());
 }
 
-template <int D, int RPT>
+template <int D, int RPT, int G>
 static int launch_d(Params p, const fpk_attn_desc* d, cudaStream_t s) {
+  static_assert(smem_bytes<D, RPT, G>() <= 227 * 1024, "shared memory of the f32 attention kernel");
   static std::atomic<int> opted[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FPK_ERR_CUDA;
   if (!opted[dev].load(std::memory_order_acquire)) {
-    if (cudaFuncSetAttribute(attn_f32_kernel<D, RPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             smem_bytes<D, RPT>()) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_f32_kernel<D, RPT, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem_bytes<D, RPT, G>()) != cudaSuccess)
       return FPK_ERR_CUDA;
     opted[dev].store(1, std::memory_order_release);
   }
@@ -190,14 +247,23 @@ static int launch_d(Params p, const fpk_attn_desc* d, cudaStream_t s) {
   p.num_mtiles = (d->seq_len + kBM - 1) / kBM;
   const int64_t blocks = d->batch * d->heads * p.num_mtiles;
   if (blocks > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
-  attn_f32_kernel<D, RPT><<<static_cast<unsigned>(blocks), kThreads, smem_bytes<D, RPT>(), s>>>(p);
+  attn_f32_kernel<D, RPT, G><<<static_cast<unsigned>(blocks), kThreads * G, smem_bytes<D, RPT, G>(), s>>>(p);
   return cudaGetLastError() == cudaSuccess ? FPK_OK : FPK_ERR_CUDA;
 }
 
+// 64-row tiles when they fill the SMs; else 16-row tiles, and when even those
+// leave SMs idle, key groups per CTA (two, or four for D <= 64 with enough key tiles)
 template <int D>
 static int launch_dd(const Params& p, const fpk_attn_desc* d, int num_sms, cudaStream_t s) {
-  const int64_t blocks64 = d->batch * d->heads * ((d->seq_len + 63) / 64);
-  return blocks64 < num_sms ? launch_d<D, 1>(p, d, s) : launch_d<D, 4>(p, d, s);
+  const int64_t bh = d->batch * d->heads;
+  if (bh * ((d->seq_len + 63) / 64) >= num_sms) return launch_d<D, 4, 1>(p, d, s);
+  const int64_t blocks16 = bh * ((d->seq_len + 15) / 16);
+  const int64_t ktiles = (d->seq_len + kBN - 1) / kBN;
+  if constexpr (D <= 64) {
+    if (ktiles >= 4 && blocks16 * 4 <= 2 * static_cast<int64_t>(num_sms)) return launch_d<D, 1, 4>(p, d, s);
+  }
+  if (ktiles >= 2 && blocks16 * 2 <= 2 * static_cast<int64_t>(num_sms)) return launch_d<D, 1, 2>(p, d, s);
+  return launch_d<D, 1, 1>(p, d, s);
 }
 
 }  // namespace attn32

@@ -220,9 +220,12 @@ def test_attention_f16_unusual_scales(scale):
     _close(out, ref.cpu().numpy(), "f16", f"scale {scale}")
 
 
-# small grids run 16-row query tiles, (4, 8, 320, 32) has >= 148 64-row tiles and runs 64-row ones
+# small grids run 16-row query tiles with their key tiles split over 4 thread groups per CTA
+# ((1, 2, 300, 64), (1, 2, 512, 16)), 2 groups ((2, 1, 77, 128), (1, 3, 65, 16): the second group
+# holds one key, (1, 4, 128, 64), (1, 1, 1000, 128)) or one ((1, 1, 1, 32)); (4, 8, 320, 32) has
+# >= 148 64-row tiles and runs 64-row ones
 @pytest.mark.parametrize("shape", [(1, 2, 300, 64), (2, 1, 77, 128), (1, 3, 65, 16), (1, 1, 1, 32),
-                                   (1, 4, 128, 64), (4, 8, 320, 32)])
+                                   (1, 4, 128, 64), (4, 8, 320, 32), (1, 2, 512, 16), (1, 1, 1000, 128)])
 def test_attention_f32_vs_oracle(shape):
     g = torch.Generator().manual_seed(sum(shape) + 1)
     q, k, v = (torch.randn(shape, generator=g) for _ in range(3))
