@@ -696,6 +696,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && mbar_wait(&bars.o_done[t], static_cast<uint32_t>(nkv - 1) & 1u, abort, p.status, limit)) {
         tc_fence_after();
         uint8_t* stage = sQ + t * C::kTileBytes;
+        // O / l as O * (1 / l): one correctly rounded reciprocal per row instead of
+        // an IEEE division per element (within 1 ulp of f32, far below the f16 store)
+        const float rl = __frcp_rn(l);
         constexpr int kChunk = D < 32 ? D : 32;
 #pragma unroll
         for (int c0 = 0; c0 < D; c0 += kChunk) {
@@ -704,8 +707,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t h2[kChunk / 2];
 #pragma unroll
           for (int c = 0; c < kChunk; c += 2)
-            h2[c / 2] = pack_half2(__fdiv_rn(__uint_as_float(orow[c]), l),
-                                   __fdiv_rn(__uint_as_float(orow[c + 1]), l));
+            h2[c / 2] = pack_half2(__fmul_rn(__uint_as_float(orow[c]), rl),
+                                   __fmul_rn(__uint_as_float(orow[c + 1]), rl));
 #pragma unroll
           for (int q = 0; q < kChunk / 8; ++q) {
             const int col = c0 + q * 8;  // first element of this 16-byte chunk
@@ -1134,6 +1137,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.epi[t][0]);
       if (!mbar_wait(&bars.epi[t][0], ne & 1u, abort, p.status, limit)) break;
+      // O / l as O * (1 / l): the epilogue lies between one item's last key tile and the
+      // next item's first, and 64 IEEE divisions per row cost as much as an exponential
+      // phase (B32 H12 S512: 443 -> 546 TFLOP/s; B8 H16 S2048: 743 -> 800)
+      const float rl = __frcp_rn(l);
       constexpr int kChunk = D < 32 ? D : 32;
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += kChunk) {
@@ -1142,7 +1149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t h2[kChunk / 2];
 #pragma unroll
         for (int c = 0; c < kChunk; c += 2)
-          h2[c / 2] = pack_half2(__fdiv_rn(__uint_as_float(orow[c]), l), __fdiv_rn(__uint_as_float(orow[c + 1]), l));
+          h2[c / 2] = pack_half2(__fmul_rn(__uint_as_float(orow[c]), rl), __fmul_rn(__uint_as_float(orow[c + 1]), rl));
 #pragma unroll
         for (int q = 0; q < kChunk / 8; ++q) {
           const int col = c0 + q * 8;
