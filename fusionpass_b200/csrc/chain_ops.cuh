@@ -43,3 +43,31 @@ __device__ __forceinline__ float op_gelu(float x) {
   const float one_plus_erf = t < 0.0f ? erfc_z : __fsub_rn(2.0f, erfc_z);
   return __fmul_rn(__fmul_rn(x, 0.5f), one_plus_erf);
 }
+
+// op_gelu of two values, the erfc polynomial on packed f32 pairs: fma.rn.f32x2 rounds each
+// lane exactly as fmaf, so both results equal op_gelu's bits
+__device__ __forceinline__ void op_gelu2(float x0, float x1, float& y0, float& y1) {
+  const float t0 = __fmul_rn(x0, 0.70710678118654752f), t1 = __fmul_rn(x1, 0.70710678118654752f);
+  const float z0 = fabsf(t0), z1 = fabsf(t1);
+  float u0, u1;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(u0) : "f"(fmaf(0.5f, z0, 1.0f)));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(u1) : "f"(fmaf(0.5f, z1, 1.0f)));
+  const float c[10] = {0.17087277f, -0.82215223f, 1.48851587f, -1.13520398f, 0.27886807f,
+                       -0.18628806f, 0.09678418f, 0.37409196f, 1.00002368f, -1.26551223f};
+  float p0 = c[0], p1 = c[0];
+#pragma unroll
+  for (int k = 1; k < 10; ++k) {
+    asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 b, {%2, %3};\n\tmov.b64 d, {%4, %4};\n\t"
+        "fma.rn.f32x2 a, a, b, d;\n\tmov.b64 {%0, %1}, a;\n\t}"
+        : "+f"(p0), "+f"(p1)
+        : "f"(u0), "f"(u1), "f"(c[k]));
+  }
+  float e0, e1;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(__fmul_rn(fmaf(-z0, z0, p0), 1.44269504088896341f)));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(__fmul_rn(fmaf(-z1, z1, p1), 1.44269504088896341f)));
+  const float ec0 = __fmul_rn(u0, e0), ec1 = __fmul_rn(u1, e1);
+  const float o0 = t0 < 0.0f ? ec0 : __fsub_rn(2.0f, ec0);
+  const float o1 = t1 < 0.0f ? ec1 : __fsub_rn(2.0f, ec1);
+  y0 = __fmul_rn(__fmul_rn(x0, 0.5f), o0);
+  y1 = __fmul_rn(__fmul_rn(x1, 0.5f), o1);
+}
