@@ -1,18 +1,25 @@
-"""``benchmark``: CUDA-event timing of eager vs fused, refused for unverified models.
+"""``benchmark``: eager vs fused device time, refused for models that failed the gate.
 
-Same gate and result type as the reference ``python/fusionpass/bench.py:43-61``:
-the verification check comes first, then the CUDA requirement; timings are the
-median of per-call CUDA-event intervals after warm-up.
+Keeps the interface of the reference ``python/fusionpass/bench.py:43-61``: the
+same ``BenchResult`` fields and the same gate order (a speedup is never
+reported for a model that has not passed ``verify_equivalence``; CPU inputs are
+refused).  Timing is this package's own: each callable runs ``iters`` times
+back to back in a few rounds bracketed by CUDA events on the current stream,
+and the per-call time is the median over rounds of the round's mean.
+``est_bytes_*`` are algorithmic bytes: every step reads each operand once and
+writes its result once (the minimum HBM traffic of the plan).
 """
 
 from __future__ import annotations
 
 from dataclasses import dataclass
+from math import prod
 
 import torch
 
-from .traffic import estimate_bytes
 from .verify import VerifyReport
+
+_ESZ = {"f16": 2, "f32": 4}
 
 
 class UnverifiedSpeedupError(RuntimeError):
@@ -32,19 +39,36 @@ class BenchResult:
     report: VerifyReport
 
 
-def _median_ms_cuda(fn, warmup: int, iters: int) -> float:
+def plan_bytes(plan: dict) -> int:
+    """Algorithmic bytes of a plan: the sum over steps of its operands' and its
+    result's sizes (each tensor moved once per step)."""
+    size = {t["name"]: prod(t["shape"]) * _ESZ[t["dtype"]] for t in plan["inputs"]}
+    total = 0
+    for st in plan["steps"]:
+        size[st["result"]] = prod(st["shape"]) * _ESZ[st["dtype"]]
+        total += sum(size.get(o, 0) for o in st["operands"]) + size[st["result"]]
+    return total
+
+
+def device_ms_per_call(fn, warmup: int, iters: int, rounds: int = 5) -> float:
+    """Per-call device time of ``fn`` on the current CUDA stream (median of the
+    per-round means of back-to-back calls)."""
     for _ in range(warmup):
         fn()
-    torch.cuda.synchronize()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(iters)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(iters)]
-    for s, e in zip(starts, ends):
-        s.record()
-        fn()
-        e.record()
-    torch.cuda.synchronize()
-    ts = sorted(s.elapsed_time(e) for s, e in zip(starts, ends))
-    return ts[len(ts) // 2]
+    stream = torch.cuda.current_stream()
+    per_round = max(1, iters // rounds)
+    means = []
+    for _ in range(rounds):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(per_round):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        means.append(e0.elapsed_time(e1) / per_round)
+    means.sort()
+    return means[len(means) // 2]
 
 
 def benchmark(model, compiled, inputs, *, unfused=None, warmup: int = 25, iters: int = 100) -> BenchResult:
@@ -55,11 +79,11 @@ def benchmark(model, compiled, inputs, *, unfused=None, warmup: int = 25, iters:
     if not inputs[0].is_cuda:
         raise RuntimeError("benchmarking requires CUDA tensors")
     with torch.no_grad():
-        eager = _median_ms_cuda(lambda: model(*inputs), warmup, iters)
-        fused = _median_ms_cuda(lambda: compiled(*inputs), warmup, iters)
+        eager = device_ms_per_call(lambda: model(*inputs), warmup, iters)
+        fused = device_ms_per_call(lambda: compiled(*inputs), warmup, iters)
     base = unfused.plan if unfused is not None else None
     return BenchResult(eager_ms=eager, fused_ms=fused, speedup=eager / fused, iters=iters,
                        eager_launches=len(base["steps"]) if base else -1,
                        fused_launches=len(compiled.plan["steps"]),
-                       est_bytes_unfused=estimate_bytes(base) if base else None,
-                       est_bytes_fused=estimate_bytes(compiled.plan), report=compiled.report)
+                       est_bytes_unfused=plan_bytes(base) if base else None,
+                       est_bytes_fused=plan_bytes(compiled.plan), report=compiled.report)

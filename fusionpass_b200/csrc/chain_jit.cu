@@ -396,8 +396,13 @@ struct Entry {
   std::vector<char> cubin;
   cudaLibrary_t lib = nullptr;
   cudaKernel_t kern = nullptr;
-  bool failed = false;
+  bool failed = false;     // NVRTC could not compile the source: permanent for the process
+  int load_failures = 0;   // module loads that failed (retried on later calls, up to a limit)
 };
+// A module load may fail for a passing reason (another thread capturing in global
+// mode, a moment without free device memory); the chain then runs on the
+// interpreter and a later call tries again, at most this many times in all.
+constexpr int kMaxLoadFailures = 3;
 
 static std::mutex g_mu;
 static std::atomic<long long> g_launches{0};
@@ -481,11 +486,19 @@ int try_launch_chain_jit(const fpk_chain_desc* d, const void* const* inputs, voi
         e.failed = true;
         return FPK_ERR_UNSUPPORTED;
       }
-      if (cudaLibraryLoadData(&e.lib, e.cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0) != cudaSuccess ||
-          cudaLibraryGetKernel(&e.kern, e.lib, "fpk_jit_chain") != cudaSuccess) {
-        cudaGetLastError();
-        e.failed = true;
+      if (e.load_failures >= kMaxLoadFailures) return FPK_ERR_UNSUPPORTED;
+      // an error the caller left pending is not ours to clear
+      const bool clean_before = cudaPeekAtLastError() == cudaSuccess;
+      bool loaded = e.lib != nullptr ||
+                    cudaLibraryLoadData(&e.lib, e.cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0) == cudaSuccess;
+      if (!loaded) e.lib = nullptr;
+      if (loaded && cudaLibraryGetKernel(&e.kern, e.lib, "fpk_jit_chain") != cudaSuccess) {
         e.kern = nullptr;
+        loaded = false;
+      }
+      if (!loaded) {
+        if (clean_before) cudaGetLastError();  // clear only the error this load raised
+        ++e.load_failures;
         return FPK_ERR_UNSUPPORTED;
       }
     }

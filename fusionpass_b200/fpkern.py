@@ -54,18 +54,29 @@ def _bcast_of(t: torch.Tensor, rows: int, cols: int, declared: str | None) -> st
         return declared
     if n == rows * cols:
         return "full"
+    if n == 1:
+        return "scalar"
+    if n == cols and n == rows:
+        # square output: the operand's shape decides, as torch broadcasting places it --
+        # [..., 1] is one value per row, [cols] or [1, cols] one value per column
+        if t.dim() >= 2 and t.shape[-1] == 1:
+            return "row"
+        if t.dim() == 1 or (t.shape[-1] == cols and t.shape[-2] == 1):
+            return "col"
+        raise ValueError(f"operand of shape {tuple(t.shape)} is ambiguous on a [{rows}, {cols}] chain: "
+                         "declare its broadcast in the descriptor's 'inputs'")
     if n == cols:
         return "col"
     if n == rows:
         return "row"
-    if n == 1:
-        return "scalar"
     raise ValueError(f"operand with {n} elements cannot broadcast onto [{rows}, {cols}]")
 
 
 def build_chain_desc(desc: Mapping[str, Any], rows: int, cols: int, in_dtypes: Sequence[int],
-                     bcasts: Sequence[str], out_dtype: int, flags: int = 0) -> _lib.ChainDesc:
-    """Fill the C descriptor for one chain launch (validated again by the library)."""
+                     bcasts: Sequence[str], out_dtype: int, flags: int = 0,
+                     mode: str | None = None) -> _lib.ChainDesc:
+    """Fill the C descriptor for one chain launch (validated again by the library).
+    ``mode`` ("flat" / "rows") overrides the descriptor's own."""
     ops = desc["ops"]
     n_in = len(in_dtypes)
     if not 1 <= n_in <= _lib.FPK_CHAIN_MAX_INPUTS:
@@ -75,7 +86,7 @@ def build_chain_desc(desc: Mapping[str, Any], rows: int, cols: int, in_dtypes: S
     d = _lib.ChainDesc()
     d.size = ctypes.sizeof(_lib.ChainDesc)
     d.version = _lib.FPK_ABI_VERSION
-    d.mode = _lib.FPK_CHAIN_ROWS if desc.get("mode") == "rows" else _lib.FPK_CHAIN_FLAT
+    d.mode = _lib.FPK_CHAIN_ROWS if (mode or desc.get("mode")) == "rows" else _lib.FPK_CHAIN_FLAT
     d.out_dtype = out_dtype
     d.rows = rows
     d.cols = cols
@@ -97,14 +108,14 @@ def build_chain_desc(desc: Mapping[str, Any], rows: int, cols: int, in_dtypes: S
     return d
 
 
-def _cached_chain_desc(desc, rows, cols, in_dtypes, bcasts, out_dtype, flags):
-    key = (id(desc), rows, cols, tuple(in_dtypes), tuple(bcasts), out_dtype, flags)
+def _cached_chain_desc(desc, rows, cols, in_dtypes, bcasts, out_dtype, flags, mode):
+    key = (id(desc), rows, cols, tuple(in_dtypes), tuple(bcasts), out_dtype, flags, mode)
     with _cache_lock:
         hit = _desc_cache.get(key)
         if hit is not None and hit[0] is desc:
             _desc_cache.move_to_end(key)
             return hit[1]
-    c = build_chain_desc(desc, rows, cols, in_dtypes, bcasts, out_dtype, flags)
+    c = build_chain_desc(desc, rows, cols, in_dtypes, bcasts, out_dtype, flags, mode)
     with _cache_lock:
         _desc_cache[key] = (desc, c)  # holding `desc` keeps its id unique while cached
         if len(_desc_cache) > _CACHE_MAX:
@@ -113,8 +124,9 @@ def _cached_chain_desc(desc, rows, cols, in_dtypes, bcasts, out_dtype, flags):
 
 
 def chain(inputs: Sequence[torch.Tensor], desc: Mapping[str, Any], out_shape, out_dtype: torch.dtype,
-          out: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
-    """Run one fused chain; ``out_shape`` is the step's result shape ([..., cols])."""
+          out: torch.Tensor | None = None, flags: int = 0, mode: str | None = None) -> torch.Tensor:
+    """Run one fused chain; ``out_shape`` is the step's result shape ([..., cols]).
+    ``mode`` ("flat" / "rows", the plan step's launch) overrides the descriptor's."""
     lib = _lib.load()
     out_shape = [int(s) for s in out_shape]
     if not inputs:
@@ -144,7 +156,7 @@ def chain(inputs: Sequence[torch.Tensor], desc: Mapping[str, Any], out_shape, ou
     elif not out.is_contiguous() or list(out.shape) != out_shape or out.dtype != out_dtype:
         raise ValueError("out must be a contiguous tensor of the step's shape and dtype")
     c = _cached_chain_desc(desc, rows, cols, [_TORCH_DT[t.dtype] for t in ins], bcasts,
-                           _TORCH_DT[out_dtype], flags)
+                           _TORCH_DT[out_dtype], flags, mode)
     ptrs = (ctypes.c_void_p * len(ins))(*[t.data_ptr() for t in ins])
     with torch.cuda.device(dev):
         rc = lib.fpk_chain_fwd(ctypes.byref(c), ptrs, len(ins), ctypes.c_void_p(out.data_ptr()),

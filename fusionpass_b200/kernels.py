@@ -210,7 +210,7 @@ def _step_desc(step: Mapping[str, Any], kernels) -> Mapping[str, Any]:
 def launch_flat(desc, ops: Sequence[Any], out, flags: int = 0):
     from . import fpkern
 
-    return fpkern.chain(ops, {**desc, "mode": "flat"}, list(out.shape), out.dtype, out=out, flags=flags)
+    return fpkern.chain(ops, desc, list(out.shape), out.dtype, out=out, flags=flags, mode="flat")
 
 
 def launch_rows(desc, ops: Sequence[Any], out, flags: int = 0):
@@ -218,7 +218,7 @@ def launch_rows(desc, ops: Sequence[Any], out, flags: int = 0):
 
     if int(out.shape[-1]) > 16384:
         raise ValueError(f"rows chain with {int(out.shape[-1])} columns exceeds the on-chip row limit")
-    return fpkern.chain(ops, {**desc, "mode": "rows"}, list(out.shape), out.dtype, out=out, flags=flags)
+    return fpkern.chain(ops, desc, list(out.shape), out.dtype, out=out, flags=flags, mode="rows")
 
 
 def launch_attention(q, k, v, out, *, scale: float, flags: int = 0, **_ignored):

@@ -1,6 +1,10 @@
 """Equivalence gate: compiled plan vs eager PyTorch, before any timing.
 
-Same contract as the reference ``python/fusionpass/verify.py:24-105``: the
+This module is the reference's gate, ``python/fusionpass/verify.py:24-105``,
+kept unchanged in behaviour on purpose: the backend is a drop-in only if the
+same gate accepts and rejects the same plans, so its checks, messages and
+tolerance table follow the reference line for line and it is not extended
+here.  The contract: the
 given inputs plus ``extra_trials`` random inputs (x2, x4, CPU generator with
 ``seed``), identical NaN/Inf patterns and Inf signs, ``|err| <= atol + rtol*|ref|``
 on finite elements, TF32 disabled in eager while checking, and the tolerance

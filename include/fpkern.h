@@ -3,9 +3,15 @@
  * fused-step families of the fusionpass plan runtime.
  *
  * Every entry point takes plain pointers, sizes and POD descriptors, never
- * allocates or frees device memory, never synchronises the stream it is given,
- * keeps no per-call state, and returns FPK_OK (0) or a negative FPK_ERR_*
- * status.  It never aborts or traps.  Device buffers are owned by the caller.
+ * allocates or frees device memory for tensors, never synchronises the stream
+ * it is given, keeps no per-call state, and returns FPK_OK (0) or a negative
+ * FPK_ERR_* status.  It never aborts or traps.  Device buffers are owned by the
+ * caller.  One exception to "no device-side setup": the first fpk_chain_fwd of
+ * a new chain program (op list, operand types, broadcast modes) compiles its
+ * kernel with NVRTC and loads it as a module (cudaLibraryLoadData), which may
+ * synchronise the device; the module is cached for the process.  Call
+ * fpk_chain_precompile and make one warm-up launch to keep this out of timed
+ * regions and stream captures (under capture the prebuilt kernels run instead).
  *
  * Reference interfaces replaced (paths within the reference project):
  *   fpk_attention_fwd  <- kernels.launch_attention + the fp_attention Triton

@@ -2,7 +2,7 @@
 
 Run once where the reference checkout is available (the tests only read the fixtures):
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py [/path/to/reference]
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py /path/to/reference
 
 It imports the reference package ``fusionpass`` from ``<reference>/python``, builds
 chain kernels with its ``KernelModuleWriter`` (the Python twin of
@@ -27,7 +27,9 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+if len(sys.argv) < 2:
+    sys.exit("usage: TRITON_INTERPRET=1 python tests/golden/make_golden.py /path/to/reference")
+REF = Path(sys.argv[1])
 sys.path.insert(0, str(REF / "python"))
 
 from fusionpass import kernels as rk  # noqa: E402  (reference package)

@@ -1,7 +1,10 @@
 """Multi-rank logic of bench.py on CPU: two gloo ranks over 127.0.0.1.
 
-The GPU run uses the same RankGroup over NCCL, one process per GPU; the data
-path has no collective (weak scaling), only the timing and pass/fail votes do.
+The GPU run uses the same RankGroup over NCCL, one process per GPU.  The
+partition is strong scaling: each rank owns a contiguous share of the global
+problem's independent units (chain rows, attention (batch, head) slices); the
+data path has no collective, and the outputs are collected afterwards with
+all_gather_into_tensor.
 """
 
 import json
@@ -54,18 +57,42 @@ def test_pass_fail_vote_is_joint(two_ranks):
     assert not any(r["one_fails"] for r in two_ranks)
 
 
-def test_weak_scaling_rate_counts_every_rank(two_ranks):
-    # 2 ranks x 100 steps x 1e6 units in 15 ms (the slowest rank)
+def test_strong_scaling_rate_counts_the_global_problem_once(two_ranks):
+    # 100 steps x 1e6 units of the whole (split) problem in 15 ms (the slowest rank)
     for r in two_ranks:
-        assert r["rate"] == pytest.approx(2 * 100 * 1.0e6 / 15e-3)
+        assert r["rate"] == pytest.approx(100 * 1.0e6 / 15e-3)
 
 
-def test_each_rank_owns_its_own_data(two_ranks):
+def test_shards_tile_the_global_problem(two_ranks):
     a, b = two_ranks
-    assert a["x_shape"] == b["x_shape"] == [4096, 4096]
-    assert a["q_shape"] == b["q_shape"] == [8, 16, 2048, 64]
-    assert a["x_head"] != b["x_head"]
-    assert a["q_head"] != b["q_head"]
+    assert a["rows"] == [0, 32] and b["rows"] == [32, 64]
+    assert a["slices"] == [0, 3] and b["slices"] == [3, 6]
+
+
+def test_gathered_outputs_equal_the_single_rank_outputs(two_ranks):
+    for r in two_ranks:
+        assert r["chain_shape"] == [64, 256] and r["chain_equal"]
+        assert r["attn_shape"] == [6, 40, 16] and r["attn_equal"]
+
+
+@pytest.mark.parametrize("n,world", [(4096, 1), (4096, 8), (128, 8), (128, 3), (5, 8), (32, 4)])
+def test_shard_range_is_a_contiguous_cover(n, world):
+    import bench
+
+    spans = [bench.shard_range(n, r, world) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == n
+    for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+        assert a1 == b0 and a0 <= a1
+    sizes = [b - a for a, b in spans]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_rotating_sets_cover_twice_the_l2():
+    import bench
+
+    for nbytes in (67_125_248, 8_396_800, 1_000, 10**10):
+        k = bench.rotating_sets(nbytes)
+        assert k >= 2 and (k * nbytes >= 2 * bench.L2_BYTES or k == 2 and nbytes >= bench.L2_BYTES)
 
 
 def test_reference_arm_runs_on_rank_zero_only(monkeypatch, capsys):
