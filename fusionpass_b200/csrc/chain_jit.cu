@@ -206,6 +206,62 @@ __device__ __forceinline__ void st8_f32(void* b, i64 off, const float* y) {
 )SRC";
 }
 
+// The element program of one 8-element vector w<u> of the flat kernel: the
+// full-shape operand values are in a<i>_<u>[8]; per-column and per-row operands
+// are loaded here, then the ops run and the result is stored.
+static void gen_vector_body(std::string& s, const fpk_chain_desc* d, int u, const char* ind) {
+  const int nin = d->n_inputs;
+  const char* dt[2] = {"f32", "f16"};
+  auto idt = [&](int i) { return dt[d->in_dtype[i] == FPK_F16 ? 1 : 0]; };
+  bool need_pos = false;
+  for (int i = 0; i < nin; ++i) need_pos |= d->in_bcast[i] == FPK_BCAST_COL || d->in_bcast[i] == FPK_BCAST_ROW;
+  if (need_pos) {
+    // 32-bit division while the vector count fits (one pass over < 2^32 vectors)
+    app(s, "%si64 row, cv;\n%sif (p.nvec <= 0xffffffffll) { const u32 q = (u32)w%d / (u32)p.ncv; row = q; cv = (i64)((u32)w%d - q * (u32)p.ncv); }\n"
+           "%selse { row = w%d / p.ncv; cv = w%d - row * p.ncv; }\n", ind, ind, u, u, ind, u, u);
+  }
+  for (int i = 0; i < nin; ++i) {
+    if (d->in_bcast[i] == FPK_BCAST_COL) app(s, "%sfloat c%d[8]; ld8c_%s(p.in[%d], cv * 8, c%d);\n", ind, i, idt(i), i, i);
+    else if (d->in_bcast[i] == FPK_BCAST_ROW) app(s, "%sconst float r%d = ld1_%s(p.in[%d], row);\n", ind, i, idt(i), i);
+  }
+  app(s, "%sfloat y[8];\n%s#pragma unroll\n%sfor (int e = 0; e < 8; e += 2) {\n", ind, ind, ind);
+  for (int h = 0; h < 2; ++h) {
+    const char* ee = h == 0 ? "e" : "e + 1";
+    for (int i = 0; i < nin; ++i) {
+      switch (d->in_bcast[i]) {
+        case FPK_BCAST_FULL: app(s, "%s  const float v%d_%d = a%d_%d[%s];\n", ind, i, h, i, u, ee); break;
+        case FPK_BCAST_COL: app(s, "%s  const float v%d_%d = c%d[%s];\n", ind, i, h, i, ee); break;
+        case FPK_BCAST_ROW: app(s, "%s  const float v%d_%d = r%d;\n", ind, i, h, i); break;
+        default: app(s, "%s  const float v%d_%d = s%d;\n", ind, i, h, i); break;
+      }
+    }
+  }
+  for (int k = 0; k < d->n_ops; ++k) {
+    const fpk_chain_op& op = d->ops[k];
+    const int dst = nin + k;
+    if (op.opcode == FPK_OP_GELU) {
+      app(s, "%s  float v%d_0, v%d_1;\n%s  op_gelu2(v%d_0, v%d_1, v%d_0, v%d_1);\n", ind, dst, dst, ind, op.src_a, op.src_a, dst, dst);
+      continue;
+    }
+    for (int h = 0; h < 2; ++h) {
+      switch (op.opcode) {
+        case FPK_OP_ADD: app(s, "%s  const float v%d_%d = __fadd_rn(v%d_%d, v%d_%d);\n", ind, dst, h, op.src_a, h, op.src_b, h); break;
+        case FPK_OP_MUL: app(s, "%s  const float v%d_%d = __fmul_rn(v%d_%d, v%d_%d);\n", ind, dst, h, op.src_a, h, op.src_b, h); break;
+        case FPK_OP_SCALE: {
+          uint32_t bits;
+          std::memcpy(&bits, &op.imm, 4);
+          app(s, "%s  const float v%d_%d = __fmul_rn(v%d_%d, __uint_as_float(0x%08xu));\n", ind, dst, h, op.src_a, h, bits);
+          break;
+        }
+        case FPK_OP_RELU: app(s, "%s  const float v%d_%d = op_relu(v%d_%d);\n", ind, dst, h, op.src_a, h); break;
+        default: app(s, "%s  const float v%d_%d = expf(v%d_%d);\n", ind, dst, h, op.src_a, h); break;
+      }
+    }
+  }
+  app(s, "%s  y[e] = v%d_0;\n%s  y[e + 1] = v%d_1;\n%s}\n", ind, d->result, ind, d->result, ind);
+  app(s, "%sst8_%s(p.out, w%d * 8, y);\n", ind, d->out_dtype == FPK_F16 ? "f16" : "f32", u);
+}
+
 // Flat chains: one pass per CTA over kBlock * kVecsPerThread consecutive vectors
 // (vector w of the run at thread w % kBlock), all full-shape loads first.
 static std::string gen_flat_source(const fpk_chain_desc* d) {
@@ -219,63 +275,18 @@ static std::string gen_flat_source(const fpk_chain_desc* d) {
   app(s, "  const i64 v0 = (i64)blockIdx.x * (%d * %d) + threadIdx.x;\n", kBlock, U);
   for (int i = 0; i < nin; ++i)
     if (d->in_bcast[i] == FPK_BCAST_SCALAR) app(s, "  const float s%d = ld1_%s(p.in[%d], 0);\n", i, idt(i), i);
-  for (int u = 0; u < U; ++u) {
-    app(s, "  const i64 w%d = v0 + %d;\n  const bool h%d = w%d < p.nvec;\n", u, u * kBlock, u, u);
-    app(s, "  const i64 off%d = w%d * 8;\n", u, u);
-  }
+  for (int u = 0; u < U; ++u) app(s, "  const i64 w%d = v0 + %d;\n", u, u * kBlock);
   for (int i = 0; i < nin; ++i) {
     if (d->in_bcast[i] != FPK_BCAST_FULL) continue;
     for (int u = 0; u < U; ++u) {
       app(s, "  float a%d_%d[8];\n", i, u);
-      app(s, "  if (h%d) ld8s_%s(p.in[%d], off%d, a%d_%d);\n", u, idt(i), i, u, i, u);
+      app(s, "  if (w%d < p.nvec) ld8s_%s(p.in[%d], w%d * 8, a%d_%d);\n", u, idt(i), i, u, i, u);
     }
   }
   for (int u = 0; u < U; ++u) {
-    app(s, "  if (h%d) {\n", u);
-    const char* ind = "    ";
-    bool need_pos = false;
-    for (int i = 0; i < nin; ++i) need_pos |= d->in_bcast[i] == FPK_BCAST_COL || d->in_bcast[i] == FPK_BCAST_ROW;
-    if (need_pos) app(s, "%sconst i64 row = w%d / p.ncv, cv = w%d - row * p.ncv;\n", ind, u, u);
-    for (int i = 0; i < nin; ++i) {
-      if (d->in_bcast[i] == FPK_BCAST_COL) app(s, "%sfloat c%d[8]; ld8c_%s(p.in[%d], cv * 8, c%d);\n", ind, i, idt(i), i, i);
-      else if (d->in_bcast[i] == FPK_BCAST_ROW) app(s, "%sconst float r%d = ld1_%s(p.in[%d], row);\n", ind, i, idt(i), i);
-    }
-    app(s, "%sfloat y[8];\n%s#pragma unroll\n%sfor (int e = 0; e < 8; e += 2) {\n", ind, ind, ind);
-    for (int h = 0; h < 2; ++h) {
-      const char* ee = h == 0 ? "e" : "e + 1";
-      for (int i = 0; i < nin; ++i) {
-        switch (d->in_bcast[i]) {
-          case FPK_BCAST_FULL: app(s, "%s  const float v%d_%d = a%d_%d[%s];\n", ind, i, h, i, u, ee); break;
-          case FPK_BCAST_COL: app(s, "%s  const float v%d_%d = c%d[%s];\n", ind, i, h, i, ee); break;
-          case FPK_BCAST_ROW: app(s, "%s  const float v%d_%d = r%d;\n", ind, i, h, i); break;
-          default: app(s, "%s  const float v%d_%d = s%d;\n", ind, i, h, i); break;
-        }
-      }
-    }
-    for (int k = 0; k < d->n_ops; ++k) {
-      const fpk_chain_op& op = d->ops[k];
-      const int dst = nin + k;
-      if (op.opcode == FPK_OP_GELU) {
-        app(s, "%s  float v%d_0, v%d_1;\n%s  op_gelu2(v%d_0, v%d_1, v%d_0, v%d_1);\n", ind, dst, dst, ind, op.src_a, op.src_a, dst, dst);
-        continue;
-      }
-      for (int h = 0; h < 2; ++h) {
-        switch (op.opcode) {
-          case FPK_OP_ADD: app(s, "%s  const float v%d_%d = __fadd_rn(v%d_%d, v%d_%d);\n", ind, dst, h, op.src_a, h, op.src_b, h); break;
-          case FPK_OP_MUL: app(s, "%s  const float v%d_%d = __fmul_rn(v%d_%d, v%d_%d);\n", ind, dst, h, op.src_a, h, op.src_b, h); break;
-          case FPK_OP_SCALE: {
-            uint32_t bits;
-            std::memcpy(&bits, &op.imm, 4);
-            app(s, "%s  const float v%d_%d = __fmul_rn(v%d_%d, __uint_as_float(0x%08xu));\n", ind, dst, h, op.src_a, h, bits);
-            break;
-          }
-          case FPK_OP_RELU: app(s, "%s  const float v%d_%d = op_relu(v%d_%d);\n", ind, dst, h, op.src_a, h); break;
-          default: app(s, "%s  const float v%d_%d = expf(v%d_%d);\n", ind, dst, h, op.src_a, h); break;
-        }
-      }
-    }
-    app(s, "%s  y[e] = v%d_0;\n%s  y[e + 1] = v%d_1;\n%s}\n", ind, d->result, ind, d->result, ind);
-    app(s, "%sst8_%s(p.out, off%d, y);\n  }\n", ind, d->out_dtype == FPK_F16 ? "f16" : "f32", u);
+    app(s, "  if (w%d < p.nvec) {\n", u);
+    gen_vector_body(s, d, u, "    ");
+    s += "  }\n";
   }
   s += "}\n";
   return s;
