@@ -7,6 +7,11 @@ Objects go to ``fusionpass_b200/_build/``; the shared library is written next to
 this file so that it travels with the source tree.  The CUDA runtime is linked
 statically and the driver's tensor-map encoder is looked up at run time, so the
 library needs nothing but the NVIDIA driver on the target machine.
+
+The torch C++ extension ``fusionpass_b200._fpkern`` (``csrc/torch_ext.cpp``, the
+binding the plan runtime launches through) is compiled with the host compiler
+against the installed torch and linked to ``libfpkern.so`` (found next to it
+through the run path ``$ORIGIN``), also in-tree.
 """
 
 from __future__ import annotations
@@ -16,6 +21,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
@@ -95,11 +101,46 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return LIB
 
 
+def extension_path() -> Path:
+    return PKG / ("_fpkern" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_extension(force: bool = False, verbose: bool = False) -> Path:
+    """Compile csrc/torch_ext.cpp into the importable module fusionpass_b200._fpkern."""
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    out = extension_path()
+    src = CSRC / "torch_ext.cpp"
+    deps = [src, ROOT / "include" / "fpkern.h", LIB]
+    if not force and not _stale(out, deps):
+        return out
+    cuda_home = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+    cxx = os.environ.get("CXX", "g++")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-w",
+           "-DTORCH_EXTENSION_NAME=_fpkern", "-DTORCH_API_INCLUDE_EXTENSION_H", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           *[f"-I{p}" for p in ce.include_paths()], f"-I{sysconfig.get_paths()['include']}",
+           f"-I{cuda_home / 'include'}", f"-I{ROOT / 'include'}",
+           str(src), "-o", str(out.with_suffix(".tmp")),
+           *[f"-L{p}" for p in ce.library_paths()], f"-L{PKG}",
+           "-lfpkern", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
+           "-Wl,-rpath,$ORIGIN"]
+    p = subprocess.run(cmd, capture_output=True, text=True)
+    if p.returncode != 0:
+        raise RuntimeError(f"building the torch extension failed:\n{p.stderr[-4000:]}")
+    os.replace(out.with_suffix(".tmp"), out)
+    if verbose:
+        print(f"[fpkern] {out}")
+    return out
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args(argv)
     build(force=a.force, verbose=True)
+    build_extension(force=a.force, verbose=True)
     return 0
 
 

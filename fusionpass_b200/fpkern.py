@@ -11,14 +11,16 @@ Descriptor format (what a plan step carries in ``attrs["desc"]``)::
 Slots ``0..n_inputs-1`` are the step's operands in order; slot ``n_inputs + k`` is
 the result of op ``k``.  All math is f32 with one rounding at the store.
 PyTorch supplies device memory and the current CUDA stream only; every fused
-step runs in ``libfpkern.so`` and there is no CPU path.
+step runs in ``libfpkern.so`` and there is no CPU path.  Launches go through the
+torch C++ extension ``fusionpass_b200._fpkern`` (``csrc/torch_ext.cpp``), which
+builds the C descriptors and takes torch's current stream; the ctypes binding in
+``_lib`` serves the ahead-of-time chain compile, the status word and the tests of
+the raw C ABI.
 """
 
 from __future__ import annotations
 
 import ctypes
-import threading
-from collections import OrderedDict
 from typing import Any, Mapping, Sequence
 
 import torch
@@ -29,9 +31,22 @@ _TORCH_DT = {torch.float32: _lib.FPK_F32, torch.float16: _lib.FPK_F16}
 _NAME_DT = {"f32": _lib.FPK_F32, "f16": _lib.FPK_F16}
 _DT_NAME = {torch.float32: "f32", torch.float16: "f16"}
 
-_cache_lock = threading.Lock()
-_desc_cache: "OrderedDict[tuple, tuple]" = OrderedDict()
-_CACHE_MAX = 256
+_ext_mod = None
+
+
+def extension():
+    """The torch C++ extension; raises (never falls back) when it is not built."""
+    global _ext_mod
+    if _ext_mod is None:
+        _lib.load()  # the extension links libfpkern.so: report a missing library first
+        try:
+            from . import _fpkern
+        except ImportError as e:
+            raise RuntimeError("the torch extension fusionpass_b200._fpkern is not built; build it with "
+                               "`python -m fusionpass_b200.build` (there is no CPU or Triton fallback for "
+                               f"fused steps): {e}") from None
+        _ext_mod = _fpkern
+    return _ext_mod
 
 
 def _stream_handle(device: torch.device) -> ctypes.c_void_p:
@@ -108,60 +123,27 @@ def build_chain_desc(desc: Mapping[str, Any], rows: int, cols: int, in_dtypes: S
     return d
 
 
-def _cached_chain_desc(desc, rows, cols, in_dtypes, bcasts, out_dtype, flags, mode):
-    key = (id(desc), rows, cols, tuple(in_dtypes), tuple(bcasts), out_dtype, flags, mode)
-    with _cache_lock:
-        hit = _desc_cache.get(key)
-        if hit is not None and hit[0] is desc:
-            _desc_cache.move_to_end(key)
-            return hit[1]
-    c = build_chain_desc(desc, rows, cols, in_dtypes, bcasts, out_dtype, flags, mode)
-    with _cache_lock:
-        _desc_cache[key] = (desc, c)  # holding `desc` keeps its id unique while cached
-        if len(_desc_cache) > _CACHE_MAX:
-            _desc_cache.popitem(last=False)
-    return c
-
-
 def chain(inputs: Sequence[torch.Tensor], desc: Mapping[str, Any], out_shape, out_dtype: torch.dtype,
           out: torch.Tensor | None = None, flags: int = 0, mode: str | None = None) -> torch.Tensor:
     """Run one fused chain; ``out_shape`` is the step's result shape ([..., cols]).
     ``mode`` ("flat" / "rows", the plan step's launch) overrides the descriptor's."""
-    lib = _lib.load()
+    ext = extension()
     out_shape = [int(s) for s in out_shape]
     if not inputs:
         raise ValueError("chain needs at least one input")
     for t in inputs:
         require_cuda(t, "chain")
     dev = inputs[0].device
-    cols = out_shape[-1] if out_shape else 1
-    numel = 1
-    for s in out_shape:
-        numel *= s
-    rows = numel // cols if cols else 0
-    declared = [spec.get("bcast") for spec in desc.get("inputs", [])] or [None] * len(inputs)
-    if len(declared) != len(inputs):
-        raise ValueError(f"descriptor lists {len(declared)} inputs, step has {len(inputs)}")
-    ins = []
-    bcasts = []
-    for t, dec in zip(inputs, declared):
+    for t in inputs:
         if t.dtype not in _TORCH_DT:
             raise ValueError(f"unsupported dtype {t.dtype}")
         if t.device != dev:
             raise ValueError("all chain operands must be on one device")
-        bcasts.append(_bcast_of(t, rows, cols, dec))
-        ins.append(t.contiguous())
     if out is None:
         out = torch.empty(out_shape, dtype=out_dtype, device=dev)
     elif not out.is_contiguous() or list(out.shape) != out_shape or out.dtype != out_dtype:
         raise ValueError("out must be a contiguous tensor of the step's shape and dtype")
-    c = _cached_chain_desc(desc, rows, cols, [_TORCH_DT[t.dtype] for t in ins], bcasts,
-                           _TORCH_DT[out_dtype], flags, mode)
-    ptrs = (ctypes.c_void_p * len(ins))(*[t.data_ptr() for t in ins])
-    with torch.cuda.device(dev):
-        rc = lib.fpk_chain_fwd(ctypes.byref(c), ptrs, len(ins), ctypes.c_void_p(out.data_ptr()),
-                               _stream_handle(dev))
-    _lib.check(rc, "fpk_chain_fwd")
+    ext.chain([t.contiguous() for t in inputs], out, desc, flags, mode)
     return out
 
 
@@ -219,38 +201,21 @@ def _bhsd(t: torch.Tensor):
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
               out: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
     """``softmax(scale * q @ k^T) @ v`` over ``[..., S, D]`` (self-attention shapes)."""
-    lib = _lib.load()
+    ext = extension()
     for t in (q, k, v):
         require_cuda(t, "attention")
     if not (q.shape == k.shape == v.shape) or not (q.dtype == k.dtype == v.dtype):
         raise ValueError("q, k, v must share one shape and dtype (FusedAttentionOp contract)")
     if q.dtype not in _TORCH_DT:
         raise ValueError(f"unsupported dtype {q.dtype}")
-    q, B, H, S, D, qs = _bhsd(q)
-    k, _, _, _, _, ks = _bhsd(k)
-    v, _, _, _, _, vs = _bhsd(v)
+    q, k, v = (_bhsd(t)[0] for t in (q, k, v))  # strided views pass as they are; others are copied
     if out is None:
         out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     elif out.shape != q.shape or out.dtype != q.dtype:
         raise ValueError("out must match q's shape and dtype")
-    out_t, _, _, _, _, os_ = _bhsd(out)
-    if out_t.data_ptr() != out.data_ptr():
+    elif _bhsd(out)[0].data_ptr() != out.data_ptr():
         raise ValueError("out must have a unit stride in its last dim and flattenable batch dims")
-    d = _lib.AttnDesc()
-    d.size = ctypes.sizeof(_lib.AttnDesc)
-    d.version = _lib.FPK_ABI_VERSION
-    d.dtype = _TORCH_DT[q.dtype]
-    d.head_dim = D
-    d.batch, d.heads, d.seq_len = B, H, S
-    d.scale = float(scale)
-    d.flags = flags
-    for i in range(3):
-        d.q_strides[i], d.k_strides[i], d.v_strides[i], d.o_strides[i] = qs[i], ks[i], vs[i], os_[i]
-    with torch.cuda.device(q.device):
-        rc = lib.fpk_attention_fwd(ctypes.byref(d), ctypes.c_void_p(q.data_ptr()),
-                                   ctypes.c_void_p(k.data_ptr()), ctypes.c_void_p(v.data_ptr()),
-                                   ctypes.c_void_p(out.data_ptr()), _stream_handle(q.device))
-    _lib.check(rc, "fpk_attention_fwd")
+    ext.attention(q, k, v, out, {"scale": float(scale)}, flags)
     return out
 
 

@@ -85,3 +85,21 @@ int main(void) {{
             ctypes.sizeof(_lib.ChainDesc), _lib.ChainDesc.in_dtype.offset, _lib.ChainDesc.ops.offset,
             ctypes.sizeof(_lib.ChainOp)]
     assert got == want
+
+
+def test_torch_extension_loads_and_refuses_cpu_tensors():
+    """fusionpass_b200._fpkern (the binding the plan runtime launches through) is
+    built in-tree, links this libfpkern.so and raises for CPU tensors."""
+    import torch
+
+    from fusionpass_b200 import fpkern
+
+    ext = fpkern.extension()
+    assert ext.version() == _lib.FPK_ABI_VERSION
+    assert Path(ext.__file__).parent == Path(_lib.library_path()).parent
+    desc = {"ops": [{"op": "relu", "a": 0}], "result": 1}
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ext.chain([torch.randn(4, 4)], torch.empty(4, 4), desc)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        q = torch.randn(1, 1, 8, 16)
+        ext.attention(q, q, q, torch.empty_like(q), {"scale": 0.25})
