@@ -21,6 +21,7 @@ produced without MLIR:
 from __future__ import annotations
 
 import operator
+import re
 from dataclasses import dataclass, field
 from typing import Any
 
@@ -76,6 +77,9 @@ class Graph:
     output: Val
     arg_tensors: list
     n_inputs: int
+    # the function's return (a pseudo-op whose operands are the returned values, so a
+    # returned value counts as used), when it returns more than one value
+    ret: "Op | None" = None
 
     def live_ops(self):
         return [o for o in self.ops if o.alive]
@@ -311,7 +315,7 @@ def _ty(v: Val) -> str:
     return "tensor<" + "x".join(str(d) for d in v.shape) + "x" + v.dtype + ">"
 
 
-def to_mlir(g: Graph) -> str:
+def to_mlir(g: Graph, name: str = "main") -> str:
     """The ``fp`` dialect text of an unfused graph (reference ``frontend.py:88-94``)."""
     names = {v: f"%arg{i}" for i, v in enumerate(g.args)}
     lines = []
@@ -336,8 +340,79 @@ def to_mlir(g: Graph) -> str:
             lines.append(f"// {r} = {op.kind} (outside the fp dialect)")
     sig = ", ".join(f"%arg{i}: {_ty(v)}" for i, v in enumerate(g.args))
     body = "\n".join("    " + ln for ln in lines)
-    return (f"module {{\n  func.func @main({sig}) -> {_ty(g.output)} {{\n{body}\n"
-            f"    return {names[g.output]} : {_ty(g.output)}\n  }}\n}}\n")
+    outs = g.ret.operands if g.ret is not None else [g.output]
+    rty = ", ".join(_ty(v) for v in outs)
+    return (f"module {{\n  func.func @{name}({sig}) -> {rty if len(outs) == 1 else '(' + rty + ')'} {{\n{body}\n"
+            f"    return {', '.join(names[v] for v in outs)} : {rty}\n  }}\n}}\n")
+
+
+_TENSOR = re.compile(r"tensor<([0-9x]+)x(f16|f32)>")
+_FUNC = re.compile(r"func\.func\s+@(\w+)\s*\((.*?)\)\s*->")
+_OPLINE = re.compile(r"^(%[\w.]+)\s*=\s*fp\.(\w+)\s+(.*)$")
+
+
+def _tensor_type(text: str) -> tuple[tuple, str]:
+    m = _TENSOR.search(text)
+    if m is None:
+        raise UnsupportedOp(f"expected a static f16/f32 tensor type in {text!r}")
+    return tuple(int(d) for d in m.group(1).split("x")), m.group(2)
+
+
+def parse_fp_mlir(text: str) -> dict[str, Graph]:
+    """Functions of an ``fp`` dialect module (the textual form ``fusionpass-opt``
+    reads: ``fp.add/mul/scale/relu/exp/softmax/transpose/matmul`` and ``return``)
+    as unfused graphs, one per ``func.func``.  The reference compiler's passes and
+    plan emitter run on this form; here the planner twin runs on it instead."""
+    funcs: dict[str, Graph] = {}
+    cur = None
+    for raw in text.splitlines():
+        line = raw.split("//", 1)[0].strip()
+        if not line:
+            continue
+        m = _FUNC.search(line)
+        if m is not None:
+            args, env = [], {}
+            for i, a in enumerate(x for x in m.group(2).split(",") if x.strip()):
+                name, ty = a.split(":", 1)
+                shape, dt = _tensor_type(ty)
+                v = Val(shape, dt, arg_index=i)
+                args.append(v)
+                env[name.strip()] = v
+            cur = (m.group(1), args, env, [])
+            continue
+        if cur is None:
+            continue
+        name, args, env, ops = cur
+        if line.startswith("return"):
+            body, _, _ = line[len("return"):].partition(":")
+            outs = [env[x.strip()] for x in body.split(",") if x.strip()]
+            g = Graph(args=args, ops=ops, output=outs[0], arg_tensors=[], n_inputs=len(args))
+            if len(outs) > 1:
+                g.ret = _new_op("return", outs, outs[0].shape, outs[0].dtype)
+            funcs[name] = g
+            cur = None
+            continue
+        m = _OPLINE.match(line)
+        if m is None:
+            continue
+        res, kind, rest = m.groups()
+        attrs = {}
+        am = re.search(r"\{(.*?)\}", rest)
+        if am is not None:
+            for kv in am.group(1).split(","):
+                k, _, v = kv.partition("=")
+                v = v.split(":")[0].strip()
+                attrs[k.strip()] = float(v) if k.strip() == "factor" else int(v)
+            rest = rest[:am.start()] + rest[am.end():]
+        head, _, types = rest.partition(" : ")
+        operands = [env[x.strip()] for x in head.split(",") if x.strip()]
+        shape, dt = _tensor_type(types.split("->")[-1])
+        if kind not in ("add", "mul", "scale", "relu", "exp", "softmax", "transpose", "matmul"):
+            raise UnsupportedOp(f"fp.{kind} is outside the fp dialect subset")
+        op = _new_op(kind, operands, shape, dt, attrs)
+        ops.append(op)
+        env[res] = op.result
+    return funcs
 
 
 # ------------------------------------------------------------- passes ---
@@ -542,7 +617,8 @@ def emit_plan(g: Graph) -> tuple[dict, K.KernelTable]:
             elif op.kind in ("reshape", "permute", "layer_norm"):
                 attrs = dict(op.attrs)
             steps.append({"kind": "torch", "op": op.kind, **base, "attrs": attrs})
-    plan = {"version": 1, "inputs": inputs, "steps": steps, "outputs": [names[g.output]]}
+    outs = g.ret.operands if g.ret is not None else [g.output]
+    plan = {"version": 1, "inputs": inputs, "steps": steps, "outputs": [names[v] for v in outs]}
     return plan, table
 
 
