@@ -15,9 +15,10 @@
 //
 // Generated flat kernel: the flattened [rows, cols/8] grid of 8-element vectors
 // (16 bytes of f16, 32 of f32) is cut into consecutive runs of 128 vectors, one
-// per 64-thread CTA, which makes a single pass: thread t takes vectors t and
-// t + 64 of its run (each load instruction of a warp covers 512 contiguous
-// bytes), loads both before computing either, and stores both.  Per-column and
+// per CTA, which makes a single pass: 128 threads with one vector each, or, for
+// chains with an exponential or GELU, 64 threads that take vectors t and t + 64
+// and load both before computing either (each load instruction of a warp covers
+// 512 contiguous bytes).  Per-column and
 // per-row operands are read per vector through the read-only cache (they stay
 // in L1/L2).  Full-shape operands are read and the result written with
 // streaming (evict-first) cache hints.  Arithmetic uses the same op definitions as the
@@ -25,7 +26,8 @@
 // adds and multiplies, so both tiers are bit-identical for flat chains.  The
 // element loop walks pairs (e, e + 1) so that GELU runs as op_gelu2, whose erfc
 // polynomial is evaluated on packed f32 pairs with per-lane results identical to
-// op_gelu (bias + GELU over f16 [16384, 3072]: 48.3 -> 45.7 us).
+// op_gelu (bias + GELU over f16 [16384, 3072]: 48.3 -> 45.7 us with the erfcc
+// form of GELU; 40.8 us with the present one).
 #include <dlfcn.h>
 #include <nvrtc.h>
 
@@ -50,13 +52,25 @@ static const char kOpsSrc[] =
     ;
 
 constexpr int kVec = 8;        // elements per thread-vector
-// One pass per 64-thread CTA with two vectors per thread: the fastest of the
-// shapes measured on B200 for a 4096 x 4096 f16 chain (12.6 us; 12.7-13.0 us for
-// 96 or 128 threads or three vectors, 13.7-18 us for 512 threads, one vector per
-// 64 threads or four; 13.3 us for the earlier persistent grid-stride kernel of
-// 16 CTAs per SM).
-constexpr int kBlock = 64;         // threads per CTA of the generated flat kernel
-constexpr int kVecsPerThread = 2;  // vectors per thread (one pass)
+
+// Geometry of the generated flat kernel: one pass, each CTA takes block * vecs
+// consecutive 8-element vectors (vector w of the run at thread w % block).  Chains
+// of adds, multiplies, scales and relus use 128 threads with one vector each;
+// chains with an exponential or GELU (tens of instructions per element) use 64
+// threads with two vectors each, whose independent work hides more latency.
+// Measured on B200 (CUDA graphs of 20 launches): relu((x + b) * s) * 0.5 + x over
+// f16 [R, 4096] 3.28 -> 3.17 / 5.33 -> 4.71 / 7.99 -> 7.58 / 13.01 -> 12.90 us for
+// R = 512 / 1024 / 2048 / 4096 with 128 x 1 instead of 64 x 2; bias + GELU over
+// [16384, 3072] 41.1 us with 64 x 2 against 42.3 with 128 x 1.  Wider CTAs (256
+// threads) or more vectors per thread (3, 4) were slower at the full cfg2 size.
+struct FlatGeom {
+  int block, vecs;
+};
+static FlatGeom flat_geom(const fpk_chain_desc* d) {
+  for (int k = 0; k < d->n_ops; ++k)
+    if (d->ops[k].opcode == FPK_OP_EXP || d->ops[k].opcode == FPK_OP_GELU) return FlatGeom{64, 2};
+  return FlatGeom{128, 1};
+}
 
 struct JitParams {
   const void* in[FPK_CHAIN_MAX_INPUTS];
@@ -272,11 +286,13 @@ static void gen_vector_body(std::string& s, const fpk_chain_desc* d, int u, cons
   app(s, "%sst8_%s(p.out, w%d * 8, y);\n", ind, d->out_dtype == FPK_F16 ? "f16" : "f32", u);
 }
 
-// Flat chains: one pass per CTA over kBlock * kVecsPerThread consecutive vectors
-// (vector w of the run at thread w % kBlock), all full-shape loads first.
+// Flat chains: one pass per CTA over block * vecs consecutive vectors (vector w
+// of the run at thread w % block, flat_geom), all full-shape loads first.
 static std::string gen_flat_source(const fpk_chain_desc* d) {
   const int nin = d->n_inputs;
-  const int U = kVecsPerThread;
+  const FlatGeom geo = flat_geom(d);
+  const int U = geo.vecs;
+  const int kBlock = geo.block;
   std::string s;
   prelude(s);
   const char* dt[2] = {"f32", "f16"};
@@ -543,10 +559,11 @@ int try_launch_chain_jit(const fpk_chain_desc* d, const void* const* inputs, voi
     block = g.block;
     if (grid > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
   } else {
-    const long long per_cta = static_cast<long long>(kBlock) * kVecsPerThread;  // one pass per CTA
+    const FlatGeom geo = flat_geom(d);
+    const long long per_cta = static_cast<long long>(geo.block) * geo.vecs;  // one pass per CTA
     grid = (p.nvec + per_cta - 1) / per_cta;
     if (grid > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
-    block = kBlock;
+    block = geo.block;
   }
   void* args[] = {&p};
   {
