@@ -814,8 +814,14 @@ def run_reference(args, world: int):
     threads = os.cpu_count() or 1
     blocks, task = oracle_chain_blocks(threads)
     with ThreadPoolExecutor(threads) as pool:
-        for _ in range(args.warmup):
+        # W passes, and passes for at least the CPU leg's sample time: a fresh
+        # process runs its first ~30 passes at a third to two thirds of the steady
+        # rate (page faults of numpy's temporaries until the allocator keeps them)
+        t0 = time.perf_counter()
+        n = 0
+        while n < args.warmup or time.perf_counter() - t0 < args.cpu_seconds:
             list(pool.map(task, blocks))
+            n += 1
         t0 = time.perf_counter()
         for _ in range(args.steps):
             list(pool.map(task, blocks))
