@@ -206,40 +206,48 @@ class RankGroup:
         tdist.all_reduce(t, op=tdist.ReduceOp.MIN)
         return bool(t.item())
 
-    def gather(self, shard: torch.Tensor) -> torch.Tensor:
-        """Concatenate every rank's equally sized shard along dim 0 (all_gather_into_tensor)."""
+    def gather(self, shard: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+        """Concatenate every rank's equally sized shard along dim 0 (all_gather_into_tensor),
+        into `out` when given."""
         if not self.dist:
             return shard
         import torch.distributed as tdist
         shard = shard.contiguous()
-        out = torch.empty((self.world * shard.shape[0],) + tuple(shard.shape[1:]), dtype=shard.dtype,
-                          device=shard.device)
+        if out is None:
+            out = torch.empty((self.world * shard.shape[0],) + tuple(shard.shape[1:]), dtype=shard.dtype,
+                              device=shard.device)
         tdist.all_gather_into_tensor(out, shard)
         return out
 
-    def timed_gather(self, shard: torch.Tensor):
-        """(gathered tensor, max-over-ranks ms) of one all-gather, CUDA events on the current stream."""
+    def timed_gather(self, shard: torch.Tensor, reps: int = 5):
+        """(gathered tensor, max-over-ranks ms per all-gather): one untimed all-gather (the
+        first of a size sets up NCCL's buffers and connections), then `reps` into the same
+        buffer between CUDA events on the current stream."""
         if self.device.type != "cuda":
             return self.gather(shard), 0.0
         stream = torch.cuda.current_stream(self.device)
+        out = self.gather(shard)
         self.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        out = self.gather(shard)
+        for _ in range(reps):
+            self.gather(shard, out)
         e1.record(stream)
         self.barrier()
-        return out, self.max(e0.elapsed_time(e1))
+        return out, self.max(e0.elapsed_time(e1)) / reps
 
 
 def gather_report(group: RankGroup, shard: torch.Tensor):
     """All-gather of the output shards, timed separately from the kernels."""
     if not group.dist:
         return shard, None
-    full, ms = group.timed_gather(shard)
+    reps = 5
+    full, ms = group.timed_gather(shard, reps)
     nbytes = full.numel() * full.element_size()
     return full, {"ms": round(ms, 4), "bytes": int(nbytes),
                   "algbw_GBps": round(nbytes / (ms * 1e-3) / 1e9, 1) if ms > 0 else None,
-                  "op": "NCCL all_gather_into_tensor of the output shards, after and outside the timed kernels"}
+                  "op": f"NCCL all_gather_into_tensor of the output shards, after and outside the timed kernels; "
+                        f"one warm-up call, then the mean of {reps}"}
 
 
 # ------------------------------------------------------------- timing
