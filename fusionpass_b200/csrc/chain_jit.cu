@@ -53,23 +53,42 @@ static const char kOpsSrc[] =
 
 constexpr int kVec = 8;        // elements per thread-vector
 
-// Geometry of the generated flat kernel: one pass, each CTA takes block * vecs
-// consecutive 8-element vectors (vector w of the run at thread w % block).  Chains
-// of adds, multiplies, scales and relus use 128 threads with one vector each;
-// chains with an exponential or GELU (tens of instructions per element) use 64
-// threads with two vectors each, whose independent work hides more latency.
-// Measured on B200 (CUDA graphs of 20 launches): relu((x + b) * s) * 0.5 + x over
-// f16 [R, 4096] 3.28 -> 3.17 / 5.33 -> 4.71 / 7.99 -> 7.58 / 13.01 -> 12.90 us for
-// R = 512 / 1024 / 2048 / 4096 with 128 x 1 instead of 64 x 2; bias + GELU over
-// [16384, 3072] 41.1 us with 64 x 2 against 42.3 with 128 x 1.  Wider CTAs (256
-// threads) or more vectors per thread (3, 4) were slower at the full cfg2 size.
-struct FlatGeom {
-  int block, vecs;
+// Geometry of the generated flat kernel: 2-D tiles of 8-element vectors.  The
+// data is viewed as rows of NCV vectors: the chain's own rows (NCV = cols / 8)
+// when a per-column or per-row operand needs an element's position, otherwise
+// virtual rows of 128 vectors over the flat index (the source then does not
+// depend on the shape).  A CTA is TW vectors wide and RPC rows high; thread
+// (tr, tc) owns vector column cv = blockIdx.x * TW + tc for the whole launch and
+// takes RPT rows spaced RPC apart in each pass: its per-column operands are loaded
+// and converted once, all its full-shape loads of a pass are issued before any is
+// used, and no index is divided.  NCV is a compile-time constant of the source.
+// The one-pass kernel this replaced (one or two vectors per thread over the flat
+// index, a position division and the per-column loads and conversions for every
+// vector) issued ~170 instructions per 16-byte vector of cfg2 and was close to
+// issue-bound (68 % issue active under ncu).  Measured on B200 (CUDA graphs of 20
+// launches): relu((x + b) * s) * 0.5 + x over f16 [R, 4096] 12.9-13.0 -> 11.8 /
+// 7.6 -> 6.9 / 4.5 -> 4.0 / 3.0 -> 3.0 us for R = 4096 / 2048 / 1024 / 512; bias +
+// GELU over [16384, 3072] 41.1 -> 37.0 us; bias + residual over [16384, 768] and
+// a two-operand chain over [4096, 4096] within 1 %.  One or two rows per thread
+// for a single full-shape operand, or four for two, measured slower.
+struct FlatTile {
+  long long ncv;  // vectors per row of the view
+  int tw, rpc, rpt;
 };
-static FlatGeom flat_geom(const fpk_chain_desc* d) {
-  for (int k = 0; k < d->n_ops; ++k)
-    if (d->ops[k].opcode == FPK_OP_EXP || d->ops[k].opcode == FPK_OP_GELU) return FlatGeom{64, 2};
-  return FlatGeom{128, 1};
+static FlatTile flat_tile(const fpk_chain_desc* d) {
+  bool pos = false;
+  int nfull = 0;
+  for (int i = 0; i < d->n_inputs; ++i) {
+    pos |= d->in_bcast[i] == FPK_BCAST_COL || d->in_bcast[i] == FPK_BCAST_ROW;
+    nfull += d->in_bcast[i] == FPK_BCAST_FULL ? 1 : 0;
+  }
+  FlatTile t;
+  t.ncv = pos ? d->cols / kVec : 128;
+  const long long nbx = (t.ncv + 127) / 128;                // CTAs across a row
+  t.tw = static_cast<int>((t.ncv + nbx - 1) / nbx);        // <= 128, as even as the row allows
+  t.rpc = t.tw >= 64 ? 1 : 128 / t.tw;                     // short rows: several per CTA
+  t.rpt = nfull <= 1 ? 4 : (nfull == 2 ? 2 : 1);           // full-shape vectors per thread and pass
+  return t;
 }
 
 struct JitParams {
@@ -215,6 +234,10 @@ __device__ __forceinline__ void ld8c_f32(const void* b, i64 off, float* a) {
   const float4 x = __ldg(p), y = __ldg(p + 1);
   a[0] = x.x; a[1] = x.y; a[2] = x.z; a[3] = x.w; a[4] = y.x; a[5] = y.y; a[6] = y.z; a[7] = y.w;
 }
+// per-column f16 operand: the raw 16 bytes, unpacked only once the full-shape loads are in flight
+__device__ __forceinline__ uint4 ldu8c_f16(const void* b, i64 off) {
+  return __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const u16*>(b) + off));
+}
 __device__ __forceinline__ float ld1_f16(const void* b, i64 i) { return h2f(__ldg(reinterpret_cast<const u16*>(b) + i)); }
 __device__ __forceinline__ float ld1_f32(const void* b, i64 i) { return __ldg(reinterpret_cast<const float*>(b) + i); }
 __device__ __forceinline__ void st8_f16(void* b, i64 off, const float* y) {
@@ -230,39 +253,27 @@ __device__ __forceinline__ void st8_f32(void* b, i64 off, const float* y) {
 )SRC";
 }
 
-// The element program of one 8-element vector w<u> of the flat kernel: the
-// full-shape operand values are in a<i>_<u>[8]; per-column and per-row operands
-// are loaded here, then the ops run and the result is stored.
-static void gen_vector_body(std::string& s, const fpk_chain_desc* d, int u, const char* ind) {
+// The element program of the thread's k-th vector of a pass (row r0 + k * RPC,
+// flat vector w<k>): full-shape values in a<i>_<k>[8], per-column values in
+// c<i>[8] (loaded once per thread), per-row values in r<i>_<k>, scalars in s<i>;
+// the ops run on element pairs and the result is stored.
+static void gen_vector_body(std::string& s, const fpk_chain_desc* d, int k, const char* ind) {
   const int nin = d->n_inputs;
-  const char* dt[2] = {"f32", "f16"};
-  auto idt = [&](int i) { return dt[d->in_dtype[i] == FPK_F16 ? 1 : 0]; };
-  bool need_pos = false;
-  for (int i = 0; i < nin; ++i) need_pos |= d->in_bcast[i] == FPK_BCAST_COL || d->in_bcast[i] == FPK_BCAST_ROW;
-  if (need_pos) {
-    // 32-bit division while the vector count fits (one pass over < 2^32 vectors)
-    app(s, "%si64 row, cv;\n%sif (p.nvec <= 0xffffffffll) { const u32 q = (u32)w%d / (u32)p.ncv; row = q; cv = (i64)((u32)w%d - q * (u32)p.ncv); }\n"
-           "%selse { row = w%d / p.ncv; cv = w%d - row * p.ncv; }\n", ind, ind, u, u, ind, u, u);
-  }
-  for (int i = 0; i < nin; ++i) {
-    if (d->in_bcast[i] == FPK_BCAST_COL) app(s, "%sfloat c%d[8]; ld8c_%s(p.in[%d], cv * 8, c%d);\n", ind, i, idt(i), i, i);
-    else if (d->in_bcast[i] == FPK_BCAST_ROW) app(s, "%sconst float r%d = ld1_%s(p.in[%d], row);\n", ind, i, idt(i), i);
-  }
   app(s, "%sfloat y[8];\n%s#pragma unroll\n%sfor (int e = 0; e < 8; e += 2) {\n", ind, ind, ind);
   for (int h = 0; h < 2; ++h) {
     const char* ee = h == 0 ? "e" : "e + 1";
     for (int i = 0; i < nin; ++i) {
       switch (d->in_bcast[i]) {
-        case FPK_BCAST_FULL: app(s, "%s  const float v%d_%d = a%d_%d[%s];\n", ind, i, h, i, u, ee); break;
+        case FPK_BCAST_FULL: app(s, "%s  const float v%d_%d = a%d_%d[%s];\n", ind, i, h, i, k, ee); break;
         case FPK_BCAST_COL: app(s, "%s  const float v%d_%d = c%d[%s];\n", ind, i, h, i, ee); break;
-        case FPK_BCAST_ROW: app(s, "%s  const float v%d_%d = r%d;\n", ind, i, h, i); break;
+        case FPK_BCAST_ROW: app(s, "%s  const float v%d_%d = r%d_%d;\n", ind, i, h, i, k); break;
         default: app(s, "%s  const float v%d_%d = s%d;\n", ind, i, h, i); break;
       }
     }
   }
-  for (int k = 0; k < d->n_ops; ++k) {
-    const fpk_chain_op& op = d->ops[k];
-    const int dst = nin + k;
+  for (int q = 0; q < d->n_ops; ++q) {
+    const fpk_chain_op& op = d->ops[q];
+    const int dst = nin + q;
     if (op.opcode == FPK_OP_GELU) {
       app(s, "%s  float v%d_0, v%d_1;\n%s  op_gelu2(v%d_0, v%d_1, v%d_0, v%d_1);\n", ind, dst, dst, ind, op.src_a, op.src_a, dst, dst);
       continue;
@@ -283,39 +294,53 @@ static void gen_vector_body(std::string& s, const fpk_chain_desc* d, int u, cons
     }
   }
   app(s, "%s  y[e] = v%d_0;\n%s  y[e + 1] = v%d_1;\n%s}\n", ind, d->result, ind, d->result, ind);
-  app(s, "%sst8_%s(p.out, w%d * 8, y);\n", ind, d->out_dtype == FPK_F16 ? "f16" : "f32", u);
+  app(s, "%sst8_%s(p.out, w%d * 8, y);\n", ind, d->out_dtype == FPK_F16 ? "f16" : "f32", k);
 }
 
-// Flat chains: one pass per CTA over block * vecs consecutive vectors (vector w
-// of the run at thread w % block, flat_geom), all full-shape loads first.
+// Flat chains: the 2-D tiles of flat_tile.  Each pass of a CTA covers RPC * RPT
+// rows of its TW-vector column block; CTAs step over the passes by gridDim.y.
 static std::string gen_flat_source(const fpk_chain_desc* d) {
   const int nin = d->n_inputs;
-  const FlatGeom geo = flat_geom(d);
-  const int U = geo.vecs;
-  const int kBlock = geo.block;
+  const FlatTile ft = flat_tile(d);
   std::string s;
   prelude(s);
   const char* dt[2] = {"f32", "f16"};
   auto idt = [&](int i) { return dt[d->in_dtype[i] == FPK_F16 ? 1 : 0]; };
-  app(s, "extern \"C\" __global__ void __launch_bounds__(%d) fpk_jit_chain(const JitParams p) {\n", kBlock);
+  app(s, "#define NCV %lldll\n#define TW %d\n#define RPC %d\n#define RPT %d\n", ft.ncv, ft.tw, ft.rpc, ft.rpt);
+  app(s, "extern \"C\" __global__ void __launch_bounds__(%d) fpk_jit_chain(const JitParams p) {\n", ft.tw * ft.rpc);
   s += kWaitPrevGrid;
-  app(s, "  const i64 v0 = (i64)blockIdx.x * (%d * %d) + threadIdx.x;\n", kBlock, U);
-  for (int i = 0; i < nin; ++i)
-    if (d->in_bcast[i] == FPK_BCAST_SCALAR) app(s, "  const float s%d = ld1_%s(p.in[%d], 0);\n", i, idt(i), i);
-  for (int u = 0; u < U; ++u) app(s, "  const i64 w%d = v0 + %d;\n", u, u * kBlock);
+  s += "  const int tc = threadIdx.x % TW, tr = threadIdx.x / TW;\n";
+  s += "  const i64 cv = (i64)blockIdx.x * TW + tc;\n";
+  s += "  if (NCV % TW != 0 && cv >= NCV) return;\n";
+  // per-column operands are read once per thread; f16 ones stay packed until the
+  // pass's full-shape loads have been issued, so their latency overlaps
   for (int i = 0; i < nin; ++i) {
-    if (d->in_bcast[i] != FPK_BCAST_FULL) continue;
-    for (int u = 0; u < U; ++u) {
-      app(s, "  float a%d_%d[8];\n", i, u);
-      app(s, "  if (w%d < p.nvec) ld8s_%s(p.in[%d], w%d * 8, a%d_%d);\n", u, idt(i), i, u, i, u);
+    if (d->in_bcast[i] == FPK_BCAST_SCALAR) app(s, "  const float s%d = ld1_%s(p.in[%d], 0);\n", i, idt(i), i);
+    if (d->in_bcast[i] != FPK_BCAST_COL) continue;
+    if (d->in_dtype[i] == FPK_F16) app(s, "  const uint4 cu%d = ldu8c_f16(p.in[%d], cv * 8);\n", i, i);
+    else app(s, "  float c%d[8]; ld8c_f32(p.in[%d], cv * 8, c%d);\n", i, i, i);
+  }
+  s += "  const i64 passes = (p.rows + RPC * RPT - 1) / (RPC * RPT);\n";
+  s += "  for (i64 pass = blockIdx.y; pass < passes; pass += gridDim.y) {\n";
+  s += "    const i64 r0 = pass * (RPC * RPT) + tr;\n";
+  for (int k = 0; k < ft.rpt; ++k) app(s, "    const i64 w%d = (r0 + %d * RPC) * NCV + cv;\n", k, k);
+  for (int i = 0; i < nin; ++i) {
+    if (d->in_bcast[i] == FPK_BCAST_FULL) {
+      for (int k = 0; k < ft.rpt; ++k)
+        app(s, "    float a%d_%d[8];\n    if (w%d < p.nvec) ld8s_%s(p.in[%d], w%d * 8, a%d_%d);\n", i, k, k, idt(i), i, k, i, k);
+    } else if (d->in_bcast[i] == FPK_BCAST_ROW) {
+      for (int k = 0; k < ft.rpt; ++k)
+        app(s, "    const float r%d_%d = w%d < p.nvec ? ld1_%s(p.in[%d], r0 + %d * RPC) : 0.0f;\n", i, k, k, idt(i), i, k);
     }
   }
-  for (int u = 0; u < U; ++u) {
-    app(s, "  if (w%d < p.nvec) {\n", u);
-    gen_vector_body(s, d, u, "    ");
-    s += "  }\n";
+  for (int i = 0; i < nin; ++i)
+    if (d->in_bcast[i] == FPK_BCAST_COL && d->in_dtype[i] == FPK_F16) app(s, "    float c%d[8]; unpack8(cu%d, c%d);\n", i, i, i);
+  for (int k = 0; k < ft.rpt; ++k) {
+    app(s, "    if (w%d < p.nvec) {\n", k);
+    gen_vector_body(s, d, k, "      ");
+    s += "    }\n";
   }
-  s += "}\n";
+  s += "  }\n}\n";
   return s;
 }
 
@@ -551,7 +576,7 @@ int try_launch_chain_jit(const fpk_chain_desc* d, const void* const* inputs, voi
   p.cols = d->cols;
   p.ncv = d->cols / kVec;
   p.nvec = d->rows * p.ncv;
-  long long grid;
+  long long grid, grid_x = 1;
   int block;
   if (kind == kRows) {
     const RowsGeom g = rows_geom(d->cols);
@@ -559,11 +584,14 @@ int try_launch_chain_jit(const fpk_chain_desc* d, const void* const* inputs, voi
     block = g.block;
     if (grid > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
   } else {
-    const FlatGeom geo = flat_geom(d);
-    const long long per_cta = static_cast<long long>(geo.block) * geo.vecs;  // one pass per CTA
-    grid = (p.nvec + per_cta - 1) / per_cta;
-    if (grid > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
-    block = geo.block;
+    const FlatTile ft = flat_tile(d);
+    p.rows = (p.nvec + ft.ncv - 1) / ft.ncv;  // rows of the tile view (virtual rows cover the flat index)
+    const long long per_pass = static_cast<long long>(ft.rpc) * ft.rpt;
+    const long long passes = (p.rows + per_pass - 1) / per_pass;
+    grid_x = (ft.ncv + ft.tw - 1) / ft.tw;
+    grid = passes < 65535 ? passes : 65535;  // CTAs loop over the rest
+    if (grid_x > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
+    block = ft.tw * ft.rpc;
   }
   void* args[] = {&p};
   {
@@ -572,7 +600,8 @@ int try_launch_chain_jit(const fpk_chain_desc* d, const void* const* inputs, voi
     // that kernel has completed and its writes are visible
     cudaLaunchConfig_t cfg;
     std::memset(&cfg, 0, sizeof(cfg));
-    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.gridDim = kind == kRows ? dim3(static_cast<unsigned>(grid))
+                                : dim3(static_cast<unsigned>(grid_x), static_cast<unsigned>(grid));
     cfg.blockDim = dim3(block);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
