@@ -32,7 +32,9 @@ def _operand(shape_kind, R, C, dt, g):
 
 
 @pytest.mark.parametrize("seed", range(6))
-@pytest.mark.parametrize("R,C", [(1, 8), (37, 40), (1000, 64), (4097, 16), (2048, 4096)])
+# (R, C): one vector; short rows several per CTA (40, 64, 16 columns); 97 and 201 vectors per row
+# (a CTA block of 97, two blocks of 101 with the last thread idle); a full-size row
+@pytest.mark.parametrize("R,C", [(1, 8), (37, 40), (1000, 64), (4097, 16), (19, 776), (33, 1608), (2048, 4096)])
 def test_random_programs_jit_equals_interpreter(seed, R, C):
     rng = np.random.default_rng(100 + seed)
     g = torch.Generator().manual_seed(seed)
