@@ -179,13 +179,22 @@ static RowsGeom rows_geom(long long cols) {
 }
 
 static void app(std::string& s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+// Appends printf-formatted text of any length.
 static void app(std::string& s, const char* fmt, ...) {
   char buf[512];
-  va_list ap;
+  va_list ap, ap2;
   va_start(ap, fmt);
+  va_copy(ap2, ap);
   const int n = vsnprintf(buf, sizeof(buf), fmt, ap);
   va_end(ap);
-  if (n > 0) s.append(buf, static_cast<size_t>(n < static_cast<int>(sizeof(buf)) ? n : sizeof(buf) - 1));
+  if (n > 0 && n < static_cast<int>(sizeof(buf))) {
+    s.append(buf, static_cast<size_t>(n));
+  } else if (n > 0) {
+    std::string big(static_cast<size_t>(n) + 1, '\0');
+    vsnprintf(&big[0], big.size(), fmt, ap2);
+    s.append(big.data(), static_cast<size_t>(n));
+  }
+  va_end(ap2);
 }
 
 // First statement of every generated kernel.  The kernels are launched with
