@@ -239,7 +239,18 @@ def launch_step(step: dict, ops: Sequence[Any], kernels):
         raise ValueError(f"unknown launch kind {launch}")
     check_device(ops[0])
     a = step["attrs"]
-    out = torch.empty(step["shape"], dtype=_torch_dtype(step["dtype"]), device=ops[0].device)
+    layout = a.get("out_layout") if launch == "attention" else None
+    if layout is not None:
+        # stored as the permutation `layout` of the step's shape (a self-inverse swap of
+        # two axes): the result is a strided view of that buffer, which the attention
+        # kernel writes through its output strides
+        perm = [int(i) for i in layout]
+        if sorted(perm) != list(range(len(step["shape"]))) or [perm[i] for i in perm] != list(range(len(perm))):
+            raise ValueError(f"out_layout {layout} is not a self-inverse permutation of the result's axes")
+        buf = torch.empty([step["shape"][i] for i in perm], dtype=_torch_dtype(step["dtype"]), device=ops[0].device)
+        out = buf.permute(*perm)
+    else:
+        out = torch.empty(step["shape"], dtype=_torch_dtype(step["dtype"]), device=ops[0].device)
     if launch == "flat":
         launch_flat(desc, ops, out)
     elif launch == "rows":

@@ -606,8 +606,16 @@ def emit_plan(g: Graph) -> tuple[dict, K.KernelTable]:
         elif op.kind == "fused_attention":
             desc = K.attention_descriptor(op.result.shape[-1])
             table[K.KERNEL_ATTENTION] = desc
+            attrs = {**K.attention_launch_attrs(op.attrs["scale"]), "desc": desc}
+            # the result's only consumer swaps heads and sequence ([B, H, S, D] -> [B, S, H, D],
+            # as before a merge of the heads): store it in that order, so the permute is a
+            # contiguous view and a following reshape copies nothing
+            users = op.result.uses
+            if (len(users) == 1 and users[0].kind == "permute" and list(users[0].attrs.get("dims", [])) == [0, 2, 1, 3]
+                    and len(op.result.shape) == 4 and g.output is not op.result):
+                attrs["out_layout"] = [0, 2, 1, 3]
             steps.append({"kind": "triton", "kernel": K.KERNEL_ATTENTION, "launch": "attention", **base,
-                          "attrs": {**K.attention_launch_attrs(op.attrs["scale"]), "desc": desc}})
+                          "attrs": attrs})
         else:
             attrs = {}
             if op.kind == "scale":
@@ -622,8 +630,34 @@ def emit_plan(g: Graph) -> tuple[dict, K.KernelTable]:
     return plan, table
 
 
+def fold_linear_bias(g: Graph) -> int:
+    """Extension graphs: an ``nn.Linear`` is traced as ``linear`` + a bias ``add`` so that
+    the add can join a chain (bias + GELU, bias + residual).  A bias add that no chain
+    took is folded back into its ``linear`` step (three operands: x, W, b), which runs
+    it in the GEMM's epilogue, as eager ``nn.Linear`` does, instead of as a separate pass
+    over the output.  Returns the number of folds."""
+    folds = 0
+    for add in list(g.ops):
+        if not add.alive or add.kind != "add" or len(add.operands) != 2:
+            continue
+        y, b = add.operands
+        lin = y.producer
+        if lin is None or not lin.alive or lin.kind != "linear" or len(lin.operands) != 2:
+            continue
+        if len(y.uses) != 1 or g.output is y or (g.ret is not None and y in g.ret.operands):
+            continue
+        if b.arg_index is None or tuple(b.shape) != (y.shape[-1],) or tuple(add.result.shape) != tuple(y.shape):
+            continue
+        new = _new_op("linear", [lin.operands[0], lin.operands[1], b], y.shape, y.dtype, lin.attrs)
+        _replace(g, add, new, [lin])
+        folds += 1
+    return folds
+
+
 def compile_graph(g: Graph, *, fuse: bool, extensions: bool = False) -> tuple[dict, K.KernelTable]:
     if fuse:
         fuse_attention(g)  # attention first so its scale/softmax are absorbed before chain fusion
         fuse_chains(g, extensions=extensions)
+        if extensions:
+            fold_linear_bias(g)
     return emit_plan(g)

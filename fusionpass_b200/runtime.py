@@ -42,7 +42,7 @@ def _run_torch(step: dict, ops: list) -> torch.Tensor:
     if op == "gelu":
         return torch.nn.functional.gelu(ops[0])
     if op == "linear":
-        return torch.nn.functional.linear(ops[0], ops[1])
+        return torch.nn.functional.linear(ops[0], ops[1], ops[2] if len(ops) == 3 else None)
     if op == "layer_norm":
         w, b = (ops[1], ops[2]) if len(ops) == 3 else (None, None)
         return torch.nn.functional.layer_norm(ops[0], attrs["normalized_shape"], w, b, attrs["eps"])

@@ -169,6 +169,34 @@ def test_bert_block_plan_shape():
     ops = sorted(tuple(o["op"] for o in s["attrs"]["desc"]["ops"]) for s in chains)
     assert ops == [("add", "add"), ("add", "add"), ("add", "gelu")]
     assert kinds.count("linear") == 6 and kinds.count("layer_norm") == 2
+    # the q / k / v biases have no chain to join: folded back into their linear steps
+    linears = [s for s in plan["steps"] if s.get("op") == "linear"]
+    assert sum(len(s["operands"]) == 3 for s in linears) == 3
+    assert not any(s.get("op") == "add" for s in plan["steps"])
+    # the attention result feeds the heads merge: stored as [B, S, H, D]
+    att = [s for s in plan["steps"] if s.get("launch") == "attention"][0]
+    assert att["attrs"]["out_layout"] == [0, 2, 1, 3]
+    validate_plan(plan)
+
+
+def test_linear_bias_fold_keeps_chained_biases():
+    class M(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.a, self.b = torch.nn.Linear(16, 16), torch.nn.Linear(16, 16)
+            self.ln = torch.nn.LayerNorm(16)
+
+        def forward(self, x):
+            return self.ln(self.b(torch.nn.functional.gelu(self.a(x))))
+
+    g = planner.trace(M().eval(), (torch.randn(4, 16),), extensions=True)
+    plan, _ = planner.compile_graph(g, fuse=True, extensions=True)
+    linears = [s for s in plan["steps"] if s.get("op") == "linear"]
+    chains = [s for s in plan["steps"] if s.get("launch") == "flat"]
+    # a's bias joins the GELU chain; b's bias add is folded into its linear
+    assert [len(s["operands"]) for s in linears] == [2, 3]
+    assert [tuple(o["op"] for o in s["attrs"]["desc"]["ops"]) for s in chains] == [("add", "gelu")]
+    assert not any(s.get("op") == "add" for s in plan["steps"])
 
 
 def test_unfused_compile_verifies_on_cpu(tmp_path):
