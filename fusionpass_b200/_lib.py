@@ -48,8 +48,10 @@ EXPORTS = (
     "fpk_chain_fwd",
     "fpk_chain_precompile",
     "fpk_chain_jit_launches",
+    "fpk_layer_norm_fwd",
     "fpk_poll_status",
 )
+FPK_LN_MAX_COLS = 2048
 
 
 class AttnDesc(ctypes.Structure):
@@ -94,6 +96,19 @@ class ChainDesc(ctypes.Structure):
         ("in_dtype", ctypes.c_int32 * FPK_CHAIN_MAX_INPUTS),
         ("in_bcast", ctypes.c_int32 * FPK_CHAIN_MAX_INPUTS),
         ("ops", ChainOp * FPK_CHAIN_MAX_OPS),
+    ]
+
+
+class LnDesc(ctypes.Structure):
+    _fields_ = [
+        ("size", ctypes.c_uint32),
+        ("version", ctypes.c_uint32),
+        ("dtype", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("rows", ctypes.c_int64),
+        ("cols", ctypes.c_int64),
+        ("eps", ctypes.c_float),
+        ("flags", ctypes.c_uint32),
     ]
 
 
@@ -146,6 +161,9 @@ def load() -> ctypes.CDLL:
         lib.fpk_chain_precompile.argtypes = [ctypes.POINTER(ChainDesc)]
         lib.fpk_chain_jit_launches.restype = ctypes.c_int64
         lib.fpk_chain_jit_launches.argtypes = []
+        lib.fpk_layer_norm_fwd.restype = ctypes.c_int
+        lib.fpk_layer_norm_fwd.argtypes = [ctypes.POINTER(LnDesc), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                           ctypes.c_void_p, ctypes.c_void_p]
         lib.fpk_poll_status.restype = ctypes.c_int
         lib.fpk_poll_status.argtypes = [ctypes.c_int, ctypes.c_void_p]
         if lib.fpk_version() != FPK_ABI_VERSION:

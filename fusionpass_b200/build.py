@@ -30,7 +30,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libfpkern.so"
-SOURCES = ["fpkern.cu", "chain.cu", "chain_jit.cu", "attention_f32.cu", "attention_tc.cu"]
+SOURCES = ["fpkern.cu", "chain.cu", "chain_jit.cu", "attention_f32.cu", "attention_tc.cu", "layer_norm.cu"]
 HEADERS = ["common.cuh", "internal.h", "tmem_ops.cuh", "chain_ops.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xptxas", "-v",

@@ -221,12 +221,52 @@ at::Tensor chain(const std::vector<at::Tensor>& inputs, at::Tensor out, const py
 
 }  // namespace
 
+// LayerNorm over the last axis of a contiguous x into out (same shape and dtype); w and b
+// per-column (length cols) or both undefined.  Returns false, leaving out untouched,
+// when the kernel does not take the shape (cols not a multiple of 8 or above
+// FPK_LN_MAX_COLS, unaligned pointers): the caller then runs its own layer_norm.
+bool layer_norm(const at::Tensor& x, const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& b,
+                at::Tensor out, double eps) {
+  require_cuda(x, "layer_norm");
+  require_cuda(out, "layer_norm");
+  if (!x.is_contiguous() || !out.is_contiguous()) value_error("layer_norm: x and out must be contiguous");
+  if (out.sizes() != x.sizes() || out.scalar_type() != x.scalar_type() || out.device() != x.device())
+    value_error("layer_norm: out must match x in shape, dtype and device");
+  if (x.dim() < 1) value_error("layer_norm: x needs at least one dim");
+  const bool affine = w.has_value() && w->defined();
+  if (affine != (b.has_value() && b->defined())) value_error("layer_norm: give both weight and bias, or neither");
+  fpk_ln_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.size = sizeof(d);
+  d.version = FPK_ABI_VERSION;
+  d.dtype = dtype_code(x);
+  d.cols = x.size(-1);
+  d.rows = d.cols > 0 ? x.numel() / d.cols : 0;
+  d.eps = static_cast<float>(eps);
+  if (affine) {
+    for (const at::Tensor* t : {&*w, &*b}) {
+      require_cuda(*t, "layer_norm");
+      if (t->numel() != d.cols || !t->is_contiguous() || t->scalar_type() != x.scalar_type() ||
+          t->device() != x.device())
+        value_error("layer_norm: weight and bias must be contiguous vectors of the last dim's size and x's dtype");
+    }
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int rc = fpk_layer_norm_fwd(&d, x.data_ptr(), affine ? w->data_ptr() : nullptr,
+                                    affine ? b->data_ptr() : nullptr, out.data_ptr(), stream_of(x));
+  if (rc == FPK_ERR_UNSUPPORTED || rc == FPK_ERR_ALIGN) return false;
+  check_status(rc, "fpk_layer_norm_fwd");
+  return true;
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "fusionpass_b200._fpkern: torch binding of libfpkern.so (sm_100a fused-step kernels)";
   m.def("version", &fpk_version, "ABI version of the loaded libfpkern.so");
   m.def("attention", &attention, "softmax(scale * q @ k^T) @ v into out on the current CUDA stream",
         pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"), pybind11::arg("out"), pybind11::arg("desc"),
         pybind11::arg("flags") = 0);
+  m.def("layer_norm", &layer_norm, "LayerNorm over the last axis into out; False if the kernel does not take the shape",
+        pybind11::arg("x"), pybind11::arg("weight"), pybind11::arg("bias"), pybind11::arg("out"), pybind11::arg("eps"));
   m.def("chain", &chain, "one fused elementwise chain into out on the current CUDA stream", pybind11::arg("inputs"),
         pybind11::arg("out"), pybind11::arg("desc"), pybind11::arg("flags") = 0,
         pybind11::arg("mode") = pybind11::none());

@@ -219,6 +219,30 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
     return out
 
 
+def layer_norm(x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor | None, eps: float,
+               out: torch.Tensor | None = None) -> torch.Tensor | None:
+    """LayerNorm over the last axis of a CUDA tensor in libfpkern.so (f16 / f32, last dim a
+    multiple of 8 and at most 2048, weight and bias of x's dtype or both None).  Returns
+    None when the kernel does not take the shape; the caller then runs torch's."""
+    ext = extension()
+    require_cuda(x, "layer_norm")
+    if x.dtype not in _TORCH_DT or x.dim() < 1:
+        return None
+    if (weight is None) != (bias is None):
+        return None
+    if weight is not None and (weight.dtype != x.dtype or bias.dtype != x.dtype):
+        return None
+    cols = x.shape[-1]
+    if cols % 8 or cols > _lib.FPK_LN_MAX_COLS or cols == 0:
+        return None
+    x = x.contiguous()
+    if out is None:
+        out = torch.empty_like(x)
+    w = weight.contiguous() if weight is not None else None
+    b = bias.contiguous() if bias is not None else None
+    return out if ext.layer_norm(x, w, b, out, float(eps)) else None
+
+
 def poll_status(device: torch.device | int | None = None) -> int:
     """Synchronise the current stream and return/clear the device status word."""
     lib = _lib.load()

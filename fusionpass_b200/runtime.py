@@ -45,6 +45,12 @@ def _run_torch(step: dict, ops: list) -> torch.Tensor:
         return torch.nn.functional.linear(ops[0], ops[1], ops[2] if len(ops) == 3 else None)
     if op == "layer_norm":
         w, b = (ops[1], ops[2]) if len(ops) == 3 else (None, None)
+        if ops[0].is_cuda and len(attrs["normalized_shape"]) == 1:
+            # over the last axis: the libfpkern kernel (None if it does not take the shape)
+            from . import fpkern
+            y = fpkern.layer_norm(ops[0], w, b, attrs["eps"])
+            if y is not None:
+                return y
         return torch.nn.functional.layer_norm(ops[0], attrs["normalized_shape"], w, b, attrs["eps"])
     if op == "reshape":
         return ops[0].reshape(attrs["shape"])

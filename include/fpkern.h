@@ -127,6 +127,24 @@ typedef struct fpk_chain_desc {
   fpk_chain_op ops[FPK_CHAIN_MAX_OPS];
 } fpk_chain_desc;
 
+/* ---- layer norm over the last axis ---------------------------------------- */
+/* Not part of the reference's fused-step interface (no reference counterpart):
+ * the `layer_norm` torch steps that plans of extension graphs carry between their
+ * fused steps (the BERT-style block) run here.  x and y are contiguous
+ * [rows, cols]; w and b are per-column vectors of length cols, both given or both
+ * NULL; one dtype for all four. */
+typedef struct fpk_ln_desc {
+  uint32_t size;      /* sizeof(fpk_ln_desc)                       */
+  uint32_t version;   /* FPK_ABI_VERSION                           */
+  int32_t  dtype;     /* FPK_F16 or FPK_F32                        */
+  int32_t  reserved;  /* 0                                         */
+  int64_t  rows;
+  int64_t  cols;      /* a multiple of 8, at most FPK_LN_MAX_COLS   */
+  float    eps;
+  uint32_t flags;     /* 0                                         */
+} fpk_ln_desc;
+#define FPK_LN_MAX_COLS 2048
+
 /* ---- entry points --------------------------------------------------------- */
 /* ABI version compiled into the library (FPK_ABI_VERSION). */
 int fpk_version(void);
@@ -166,6 +184,13 @@ int fpk_chain_precompile(const fpk_chain_desc* d);
  * launched through run-time compiled kernels (the rest ran on the prebuilt
  * interpreter kernels). */
 int64_t fpk_chain_jit_launches(void);
+
+/* y = (x - mean) / sqrt(var + eps) * w + b over each row (mean and biased variance
+ * in f32), enqueued on `stream`.  FPK_ERR_UNSUPPORTED for cols outside
+ * (0, FPK_LN_MAX_COLS] or not a multiple of 8 (the caller keeps its own
+ * implementation for those); FPK_ERR_ALIGN for pointers not 16-byte aligned. */
+int fpk_layer_norm_fwd(const fpk_ln_desc* d, const void* x, const void* w, const void* b, void* y,
+                       void* stream);
 
 /* Synchronise `stream`, then return and clear the device status word of
  * `device` (FPK_OK or the first FPK_ERR_* a kernel recorded, e.g. a timeout). */
