@@ -622,7 +622,7 @@ def emit_plan(g: Graph) -> tuple[dict, K.KernelTable]:
                 attrs["factor"] = float(op.attrs["factor"])
             elif op.kind == "softmax":
                 attrs["axis"] = int(op.attrs["axis"])
-            elif op.kind in ("reshape", "permute", "layer_norm"):
+            elif op.kind in ("reshape", "permute", "layer_norm", "cat", "narrow"):
                 attrs = dict(op.attrs)
             steps.append({"kind": "torch", "op": op.kind, **base, "attrs": attrs})
     outs = g.ret.operands if g.ret is not None else [g.output]
@@ -654,10 +654,47 @@ def fold_linear_bias(g: Graph) -> int:
     return folds
 
 
+def merge_sibling_linears(g: Graph) -> int:
+    """Extension graphs: ``linear`` steps (with their biases) that read the same input —
+    the q / k / v projections of an attention block — become one GEMM over the
+    concatenated weights and biases (``cat`` steps, a few MB per call) followed by one
+    ``narrow`` view per original output, so the projections run as one wider GEMM and the
+    attention reads its operands straight out of its result.  Returns the number of
+    linear steps merged away."""
+    merged = 0
+    groups: dict[int, list[Op]] = {}
+    for op in g.ops:
+        if op.alive and op.kind == "linear" and len(op.operands) == 3:
+            w, b = op.operands[1], op.operands[2]
+            if w.arg_index is not None and b.arg_index is not None and len(w.shape) == 2:
+                groups.setdefault(id(op.operands[0]), []).append(op)
+    for sibs in groups.values():
+        if len(sibs) < 2 or len({(o.result.dtype, o.operands[1].shape[1]) for o in sibs}) != 1:
+            continue
+        x = sibs[0].operands[0]
+        dt = sibs[0].result.dtype
+        outs = [o.operands[1].shape[0] for o in sibs]
+        total = sum(outs)
+        lead = tuple(sibs[0].result.shape[:-1])
+        cat_w = _new_op("cat", [o.operands[1] for o in sibs], (total, sibs[0].operands[1].shape[1]), dt, {"dim": 0})
+        cat_b = _new_op("cat", [o.operands[2] for o in sibs], (total,), dt, {"dim": 0})
+        lin = _new_op("linear", [x, cat_w.result, cat_b.result], lead + (total,), dt)
+        at = g.ops.index(sibs[0])
+        g.ops[at:at] = [cat_w, cat_b, lin]
+        start = 0
+        for o, n in zip(sibs, outs):
+            view = _new_op("narrow", [lin.result], o.result.shape, dt, {"dim": -1, "start": start, "length": n})
+            _replace(g, o, view, [])
+            start += n
+        merged += len(sibs) - 1
+    return merged
+
+
 def compile_graph(g: Graph, *, fuse: bool, extensions: bool = False) -> tuple[dict, K.KernelTable]:
     if fuse:
         fuse_attention(g)  # attention first so its scale/softmax are absorbed before chain fusion
         fuse_chains(g, extensions=extensions)
         if extensions:
             fold_linear_bias(g)
+            merge_sibling_linears(g)
     return emit_plan(g)

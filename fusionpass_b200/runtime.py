@@ -54,6 +54,10 @@ def _run_torch(step: dict, ops: list) -> torch.Tensor:
         return torch.nn.functional.layer_norm(ops[0], attrs["normalized_shape"], w, b, attrs["eps"])
     if op == "reshape":
         return ops[0].reshape(attrs["shape"])
+    if op == "cat":
+        return torch.cat(ops, dim=attrs["dim"])
+    if op == "narrow":
+        return ops[0].narrow(attrs["dim"], attrs["start"], attrs["length"])
     if op == "permute":
         return ops[0].permute(*attrs["dims"])
     raise ValueError(f"unknown torch op in plan: {op}")

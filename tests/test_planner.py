@@ -168,10 +168,16 @@ def test_bert_block_plan_shape():
     chains = [s for s in plan["steps"] if s.get("launch") == "flat"]
     ops = sorted(tuple(o["op"] for o in s["attrs"]["desc"]["ops"]) for s in chains)
     assert ops == [("add", "add"), ("add", "add"), ("add", "gelu")]
-    assert kinds.count("linear") == 6 and kinds.count("layer_norm") == 2
-    # the q / k / v biases have no chain to join: folded back into their linear steps
+    assert kinds.count("layer_norm") == 2
+    # the q / k / v biases have no chain to join: folded back into their linear steps, and the
+    # three projections of x merged into one GEMM over the concatenated weights and biases
     linears = [s for s in plan["steps"] if s.get("op") == "linear"]
-    assert sum(len(s["operands"]) == 3 for s in linears) == 3
+    assert len(linears) == 4 and [len(s["operands"]) for s in linears] == [3, 2, 2, 2]
+    assert linears[0]["shape"][-1] == 3 * 768
+    cats = [s for s in plan["steps"] if s.get("op") == "cat"]
+    assert [c["shape"] for c in cats] == [[3 * 768, 768], [3 * 768]]
+    narrows = [s["attrs"] for s in plan["steps"] if s.get("op") == "narrow"]
+    assert [(a["start"], a["length"]) for a in narrows] == [(0, 768), (768, 768), (1536, 768)]
     assert not any(s.get("op") == "add" for s in plan["steps"])
     # the attention result feeds the heads merge: stored as [B, S, H, D]
     att = [s for s in plan["steps"] if s.get("launch") == "attention"][0]
