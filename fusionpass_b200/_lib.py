@@ -49,6 +49,7 @@ EXPORTS = (
     "fpk_chain_precompile",
     "fpk_chain_jit_launches",
     "fpk_layer_norm_fwd",
+    "fpk_add_layer_norm_fwd",
     "fpk_poll_status",
 )
 FPK_LN_MAX_COLS = 2048
@@ -161,6 +162,10 @@ def load() -> ctypes.CDLL:
         lib.fpk_chain_precompile.argtypes = [ctypes.POINTER(ChainDesc)]
         lib.fpk_chain_jit_launches.restype = ctypes.c_int64
         lib.fpk_chain_jit_launches.argtypes = []
+        lib.fpk_add_layer_norm_fwd.restype = ctypes.c_int
+        lib.fpk_add_layer_norm_fwd.argtypes = [ctypes.POINTER(LnDesc), ctypes.POINTER(ctypes.c_void_p),
+                                               ctypes.POINTER(ctypes.c_int32), ctypes.c_int, ctypes.c_void_p,
+                                               ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         lib.fpk_layer_norm_fwd.restype = ctypes.c_int
         lib.fpk_layer_norm_fwd.argtypes = [ctypes.POINTER(LnDesc), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_void_p, ctypes.c_void_p]

@@ -134,16 +134,35 @@ int fpk_chain_precompile(const fpk_chain_desc* d) {
 
 int64_t fpk_chain_jit_launches(void) { return static_cast<int64_t>(fpk::chain_jit_launches()); }
 
-int fpk_layer_norm_fwd(const fpk_ln_desc* d, const void* x, const void* w, const void* b, void* y,
-                       void* stream) {
+namespace {
+int ln_checks(const fpk_ln_desc* d, const void* w, const void* b, const void* y) {
   if (!d || d->size != sizeof(fpk_ln_desc) || d->version != FPK_ABI_VERSION) return FPK_ERR_INVALID;
   if ((d->dtype != FPK_F16 && d->dtype != FPK_F32) || d->rows < 0 || d->reserved != 0 || d->flags != 0)
     return FPK_ERR_INVALID;
-  if (!x || !y || (w == nullptr) != (b == nullptr) || !(d->eps >= 0.0f)) return FPK_ERR_INVALID;
-  fpk::DeviceInfo dev;
-  const int rc = fpk::current_device_info(&dev);
+  if (!y || (w == nullptr) != (b == nullptr) || !(d->eps >= 0.0f)) return FPK_ERR_INVALID;
+  return FPK_OK;
+}
+}  // namespace
+
+int fpk_layer_norm_fwd(const fpk_ln_desc* d, const void* x, const void* w, const void* b, void* y,
+                       void* stream) {
+  int rc = ln_checks(d, w, b, y);
   if (rc != FPK_OK) return rc;
-  return fpk::launch_layer_norm(d, x, w, b, y, static_cast<cudaStream_t>(stream));
+  if (!x) return FPK_ERR_INVALID;
+  fpk::DeviceInfo dev;
+  if ((rc = fpk::current_device_info(&dev)) != FPK_OK) return rc;
+  const int32_t full = FPK_BCAST_FULL;
+  return fpk::launch_layer_norm(d, &x, &full, 1, w, b, y, static_cast<cudaStream_t>(stream));
+}
+
+int fpk_add_layer_norm_fwd(const fpk_ln_desc* d, const void* const* addends, const int32_t* bcast, int n_addends,
+                           const void* w, const void* b, void* y, void* stream) {
+  int rc = ln_checks(d, w, b, y);
+  if (rc != FPK_OK) return rc;
+  if (!addends || !bcast || n_addends < 1 || n_addends > 4) return FPK_ERR_INVALID;
+  fpk::DeviceInfo dev;
+  if ((rc = fpk::current_device_info(&dev)) != FPK_OK) return rc;
+  return fpk::launch_layer_norm(d, addends, bcast, n_addends, w, b, y, static_cast<cudaStream_t>(stream));
 }
 
 int fpk_poll_status(int device, void* stream) {

@@ -37,7 +37,7 @@ int launch_attention_f32(const fpk_attn_desc* d, const void* q, const void* k, c
 int launch_attention_tc(const fpk_attn_desc* d, const void* q, const void* k, const void* v,
                         void* o, cudaStream_t stream, const DeviceInfo& dev);
 
-int launch_layer_norm(const fpk_ln_desc* d, const void* x, const void* w, const void* b, void* y,
-                      cudaStream_t stream);
+int launch_layer_norm(const fpk_ln_desc* d, const void* const* addends, const int32_t* bcast, int n_addends,
+                      const void* w, const void* b, void* y, cudaStream_t stream);
 
 }  // namespace fpk

@@ -1,5 +1,5 @@
-// LayerNorm over the last axis for the `layer_norm` torch steps of extension plans
-// (the BERT-style block: unfused LayerNorm between the fused chains).
+// LayerNorm over the last axis for the `layer_norm` / `add_layer_norm` torch steps of
+// extension plans (the BERT-style block), the latter with the add chain that feeds it.
 //
 // y = (x - mean) * rstd * w + b over each row of a contiguous [rows, cols] tensor,
 // mean and biased variance in f32, rstd = 1 / sqrt(var + eps) correctly rounded
@@ -70,22 +70,46 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// The row's input is the sum of 1..4 addends, each full-shape ([rows, cols]) or per
+// column (length cols), added in f32 in the given order (a residual and bias added
+// before the normalisation: the add chain that feeds a LayerNorm, fused into it).
+struct Addends {
+  const void* p[4];
+  uint32_t col_mask;  // bit i: addend i is per column
+  int n;
+};
+
+template <typename T>
+__device__ __forceinline__ void load_addend(const Addends& a, int i, int64_t row_off, int col, float* v) {
+  const T* base = static_cast<const T*>(a.p[i]);
+  if ((a.col_mask >> i) & 1u) load8c(base + col, v);
+  else load8(base + row_off + col, v);
+}
+
 template <typename T, int VPL>
-__global__ void __launch_bounds__(32 * kRowsPerCta) layer_norm_kernel(const T* __restrict__ x,
-                                                                      const T* __restrict__ w,
+__global__ void __launch_bounds__(32 * kRowsPerCta) layer_norm_kernel(const Addends a, const T* __restrict__ w,
                                                                       const T* __restrict__ b, T* __restrict__ y,
                                                                       int64_t rows, int cols, float eps) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerCta + (threadIdx.x >> 5);
   if (row >= rows) return;  // whole warps leave together: the shuffles below stay converged
   const int nv = cols / 8;
-  const T* xr = x + row * cols;
+  const int64_t row_off = row * cols;
   float v[VPL * 8];
 #pragma unroll
   for (int k = 0; k < VPL; ++k) {
     const int vi = k * 32 + lane;
     if (vi < nv) {
-      load8(xr + vi * 8, v + k * 8);
+      load_addend<T>(a, 0, row_off, vi * 8, v + k * 8);
+#pragma unroll
+      for (int i = 1; i < 4; ++i) {  // constant indices keep the addend pointers in registers
+        if (i < a.n) {
+          float t[8];
+          load_addend<T>(a, i, row_off, vi * 8, t);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[k * 8 + e] = __fadd_rn(v[k * 8 + e], t[e]);
+        }
+      }
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[k * 8 + e] = 0.0f;
@@ -109,7 +133,7 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) layer_norm_kernel(const T* _
   }
   const float var = __fmul_rn(warp_sum(q), inv_n);
   const float rstd = __frsqrt_rn(__fadd_rn(var, eps));
-  T* yr = y + row * cols;
+  T* yr = y + row_off;
 #pragma unroll
   for (int k = 0; k < VPL; ++k) {
     const int vi = k * 32 + lane;
@@ -129,43 +153,51 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) layer_norm_kernel(const T* _
 }
 
 template <typename T, int VPL>
-static int launch_vpl(const fpk_ln_desc* d, const void* x, const void* w, const void* b, void* y,
+static int launch_vpl(const fpk_ln_desc* d, const Addends& a, const void* w, const void* b, void* y,
                       cudaStream_t s) {
   const int64_t grid = (d->rows + kRowsPerCta - 1) / kRowsPerCta;
   if (grid > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
   layer_norm_kernel<T, VPL><<<static_cast<unsigned>(grid), 32 * kRowsPerCta, 0, s>>>(
-      static_cast<const T*>(x), static_cast<const T*>(w), static_cast<const T*>(b), static_cast<T*>(y), d->rows,
-      static_cast<int>(d->cols), d->eps);
+      a, static_cast<const T*>(w), static_cast<const T*>(b), static_cast<T*>(y), d->rows, static_cast<int>(d->cols),
+      d->eps);
   return cudaGetLastError() == cudaSuccess ? FPK_OK : FPK_ERR_CUDA;
 }
 
 template <typename T>
-static int launch_t(const fpk_ln_desc* d, const void* x, const void* w, const void* b, void* y, cudaStream_t s) {
+static int launch_t(const fpk_ln_desc* d, const Addends& a, const void* w, const void* b, void* y, cudaStream_t s) {
   const int vpl = static_cast<int>((d->cols / 8 + 31) / 32);
   switch (vpl) {
-    case 1: return launch_vpl<T, 1>(d, x, w, b, y, s);
-    case 2: return launch_vpl<T, 2>(d, x, w, b, y, s);
-    case 3: return launch_vpl<T, 3>(d, x, w, b, y, s);
-    case 4: return launch_vpl<T, 4>(d, x, w, b, y, s);
-    case 5: return launch_vpl<T, 5>(d, x, w, b, y, s);
-    case 6: return launch_vpl<T, 6>(d, x, w, b, y, s);
-    case 7: return launch_vpl<T, 7>(d, x, w, b, y, s);
-    case 8: return launch_vpl<T, 8>(d, x, w, b, y, s);
+    case 1: return launch_vpl<T, 1>(d, a, w, b, y, s);
+    case 2: return launch_vpl<T, 2>(d, a, w, b, y, s);
+    case 3: return launch_vpl<T, 3>(d, a, w, b, y, s);
+    case 4: return launch_vpl<T, 4>(d, a, w, b, y, s);
+    case 5: return launch_vpl<T, 5>(d, a, w, b, y, s);
+    case 6: return launch_vpl<T, 6>(d, a, w, b, y, s);
+    case 7: return launch_vpl<T, 7>(d, a, w, b, y, s);
+    case 8: return launch_vpl<T, 8>(d, a, w, b, y, s);
     default: return FPK_ERR_UNSUPPORTED;
   }
 }
 
 }  // namespace ln
 
-int launch_layer_norm(const fpk_ln_desc* d, const void* x, const void* w, const void* b, void* y,
-                      cudaStream_t stream) {
+int launch_layer_norm(const fpk_ln_desc* d, const void* const* addends, const int32_t* bcast, int n_addends,
+                      const void* w, const void* b, void* y, cudaStream_t stream) {
   using namespace ln;
   if (d->cols <= 0 || d->cols % 8 || d->cols > 32 * 8 * kMaxVpl) return FPK_ERR_UNSUPPORTED;
+  if (n_addends < 1 || n_addends > 4) return FPK_ERR_INVALID;
+  Addends a{};
+  a.n = n_addends;
+  uintptr_t mis = reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(b);
+  for (int i = 0; i < n_addends; ++i) {
+    if (!addends[i] || (bcast[i] != FPK_BCAST_FULL && bcast[i] != FPK_BCAST_COL)) return FPK_ERR_INVALID;
+    a.p[i] = addends[i];
+    if (bcast[i] == FPK_BCAST_COL) a.col_mask |= 1u << i;
+    mis |= reinterpret_cast<uintptr_t>(addends[i]);
+  }
   if (d->rows == 0) return FPK_OK;
-  const uintptr_t mis = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
-                        reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(b);
   if (mis % 16) return FPK_ERR_ALIGN;
-  return d->dtype == FPK_F16 ? launch_t<__half>(d, x, w, b, y, stream) : launch_t<float>(d, x, w, b, y, stream);
+  return d->dtype == FPK_F16 ? launch_t<__half>(d, a, w, b, y, stream) : launch_t<float>(d, a, w, b, y, stream);
 }
 
 }  // namespace fpk

@@ -259,6 +259,52 @@ bool layer_norm(const at::Tensor& x, const c10::optional<at::Tensor>& w, const c
   return true;
 }
 
+// LayerNorm over the last axis of the sum of 1..4 addends (each of out's shape, or a
+// vector of its last dim's size, added in order) into out.  False, leaving out
+// untouched, when the kernel does not take the shape.
+bool add_layer_norm(const std::vector<at::Tensor>& addends, const c10::optional<at::Tensor>& w,
+                    const c10::optional<at::Tensor>& b, at::Tensor out, double eps) {
+  require_cuda(out, "add_layer_norm");
+  if (!out.is_contiguous() || out.dim() < 1) value_error("add_layer_norm: out must be contiguous with rank >= 1");
+  if (addends.empty() || addends.size() > 4) value_error("add_layer_norm: 1 to 4 addends");
+  const bool affine = w.has_value() && w->defined();
+  if (affine != (b.has_value() && b->defined())) value_error("add_layer_norm: give both weight and bias, or neither");
+  fpk_ln_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.size = sizeof(d);
+  d.version = FPK_ABI_VERSION;
+  d.dtype = dtype_code(out);
+  d.cols = out.size(-1);
+  d.rows = d.cols > 0 ? out.numel() / d.cols : 0;
+  d.eps = static_cast<float>(eps);
+  const void* ptrs[4];
+  int32_t bc[4];
+  for (size_t i = 0; i < addends.size(); ++i) {
+    const at::Tensor& t = addends[i];
+    require_cuda(t, "add_layer_norm");
+    if (!t.is_contiguous() || t.scalar_type() != out.scalar_type() || t.device() != out.device())
+      value_error("add_layer_norm: addends must be contiguous, of out's dtype and device");
+    if (t.sizes() == out.sizes()) bc[i] = FPK_BCAST_FULL;
+    else if (t.numel() == d.cols && t.size(-1) == d.cols) bc[i] = FPK_BCAST_COL;
+    else value_error("add_layer_norm: an addend has neither out's shape nor its last dim's size");
+    ptrs[i] = t.data_ptr();
+  }
+  if (affine) {
+    for (const at::Tensor* t : {&*w, &*b}) {
+      require_cuda(*t, "add_layer_norm");
+      if (t->numel() != d.cols || !t->is_contiguous() || t->scalar_type() != out.scalar_type() ||
+          t->device() != out.device())
+        value_error("add_layer_norm: weight and bias must be contiguous vectors of the last dim's size and out's dtype");
+    }
+  }
+  const c10::cuda::CUDAGuard guard(out.device());
+  const int rc = fpk_add_layer_norm_fwd(&d, ptrs, bc, static_cast<int>(addends.size()), affine ? w->data_ptr() : nullptr,
+                                        affine ? b->data_ptr() : nullptr, out.data_ptr(), stream_of(out));
+  if (rc == FPK_ERR_UNSUPPORTED || rc == FPK_ERR_ALIGN) return false;
+  check_status(rc, "fpk_add_layer_norm_fwd");
+  return true;
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "fusionpass_b200._fpkern: torch binding of libfpkern.so (sm_100a fused-step kernels)";
   m.def("version", &fpk_version, "ABI version of the loaded libfpkern.so");
@@ -267,6 +313,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("flags") = 0);
   m.def("layer_norm", &layer_norm, "LayerNorm over the last axis into out; False if the kernel does not take the shape",
         pybind11::arg("x"), pybind11::arg("weight"), pybind11::arg("bias"), pybind11::arg("out"), pybind11::arg("eps"));
+  m.def("add_layer_norm", &add_layer_norm,
+        "LayerNorm over the last axis of the sum of the addends into out; False if the kernel does not take the shape",
+        pybind11::arg("addends"), pybind11::arg("weight"), pybind11::arg("bias"), pybind11::arg("out"),
+        pybind11::arg("eps"));
   m.def("chain", &chain, "one fused elementwise chain into out on the current CUDA stream", pybind11::arg("inputs"),
         pybind11::arg("out"), pybind11::arg("desc"), pybind11::arg("flags") = 0,
         pybind11::arg("mode") = pybind11::none());

@@ -243,6 +243,37 @@ def layer_norm(x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor 
     return out if ext.layer_norm(x, w, b, out, float(eps)) else None
 
 
+def add_layer_norm(addends, weight: torch.Tensor | None, bias: torch.Tensor | None, eps: float,
+                   out: torch.Tensor | None = None) -> torch.Tensor | None:
+    """LayerNorm over the last axis of ``addends[0] + addends[1] + ...`` (1 to 4 CUDA
+    tensors of the result's shape or vectors of its last dim, summed in f32 in order) in
+    libfpkern.so; None when the kernel does not take the shapes or dtypes."""
+    ext = extension()
+    addends = list(addends)
+    if not 1 <= len(addends) <= 4:
+        return None
+    full = [t for t in addends if t.dim() >= 1 and t.numel() != t.shape[-1]] or addends[:1]
+    shape = full[0].shape
+    dt = addends[0].dtype
+    for t in addends:
+        require_cuda(t, "add_layer_norm")
+        if t.dtype != dt or (tuple(t.shape) != tuple(shape) and t.numel() != shape[-1]):
+            return None
+    if dt not in _TORCH_DT or (weight is None) != (bias is None):
+        return None
+    if weight is not None and (weight.dtype != dt or bias.dtype != dt):
+        return None
+    cols = shape[-1]
+    if cols % 8 or cols > _lib.FPK_LN_MAX_COLS or cols == 0:
+        return None
+    addends = [t.contiguous() for t in addends]
+    if out is None:
+        out = torch.empty(shape, dtype=dt, device=addends[0].device)
+    w = weight.contiguous() if weight is not None else None
+    b = bias.contiguous() if bias is not None else None
+    return out if ext.add_layer_norm(addends, w, b, out, float(eps)) else None
+
+
 def poll_status(device: torch.device | int | None = None) -> int:
     """Synchronise the current stream and return/clear the device status word."""
     lib = _lib.load()

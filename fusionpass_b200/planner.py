@@ -622,7 +622,7 @@ def emit_plan(g: Graph) -> tuple[dict, K.KernelTable]:
                 attrs["factor"] = float(op.attrs["factor"])
             elif op.kind == "softmax":
                 attrs["axis"] = int(op.attrs["axis"])
-            elif op.kind in ("reshape", "permute", "layer_norm", "cat", "narrow"):
+            elif op.kind in ("reshape", "permute", "layer_norm", "add_layer_norm", "cat", "narrow"):
                 attrs = dict(op.attrs)
             steps.append({"kind": "torch", "op": op.kind, **base, "attrs": attrs})
     outs = g.ret.operands if g.ret is not None else [g.output]
@@ -652,6 +652,45 @@ def fold_linear_bias(g: Graph) -> int:
         _replace(g, add, new, [lin])
         folds += 1
     return folds
+
+
+def fuse_add_layer_norm(g: Graph) -> int:
+    """Extension graphs: a chain of adds (a residual plus a bias) whose only consumer is a
+    LayerNorm over the last axis becomes one ``add_layer_norm`` step that sums the chain's
+    operands in the chain's order and normalises, so the sum is never written out.  Only
+    where the LayerNorm kernel takes the shape (last dim a multiple of 8, at most 2048,
+    one dtype); returns the number of fusions."""
+    fused = 0
+    for ln in list(g.ops):
+        if not ln.alive or ln.kind != "layer_norm" or len(ln.operands) not in (1, 3):
+            continue
+        x = ln.operands[0]
+        ch = x.producer
+        cols = x.shape[-1] if x.shape else 0
+        if (ch is None or not ch.alive or ch.kind != "fused_chain" or len(x.uses) != 1 or g.output is x
+                or list(ln.attrs.get("normalized_shape", [])) != [cols] or cols % 8 or cols > 2048 or cols == 0):
+            continue
+        if g.ret is not None and x in g.ret.operands:
+            continue
+        order = []
+        ok = all(kind == "add" for kind, _, _ in ch.body)
+        for k, (_, refs, _) in enumerate(ch.body if ok else []):
+            temps = [r for r in refs if r[0] == "t"]
+            args = [r[1] for r in refs if r[0] == "a"]
+            if (k == 0 and temps) or (k > 0 and temps != [("t", k - 1)]):
+                ok = False
+                break
+            order += args
+        ext = ch.operands
+        if (not ok or sorted(order) != list(range(len(ext))) or len(ext) > 4
+                or any(v.dtype != x.dtype or _bcast_mode(v, x.shape) not in ("full", "col") for v in ext)
+                or any(v.dtype != x.dtype for v in ln.operands[1:])):
+            continue
+        new = _new_op("add_layer_norm", [ext[i] for i in order] + list(ln.operands[1:]), ln.result.shape,
+                      ln.result.dtype, {**ln.attrs, "n_addends": len(order)})
+        _replace(g, ln, new, [ch])
+        fused += 1
+    return fused
 
 
 def merge_sibling_linears(g: Graph) -> int:
@@ -697,4 +736,5 @@ def compile_graph(g: Graph, *, fuse: bool, extensions: bool = False) -> tuple[di
         if extensions:
             fold_linear_bias(g)
             merge_sibling_linears(g)
+            fuse_add_layer_norm(g)
     return emit_plan(g)

@@ -52,6 +52,19 @@ def _run_torch(step: dict, ops: list) -> torch.Tensor:
             if y is not None:
                 return y
         return torch.nn.functional.layer_norm(ops[0], attrs["normalized_shape"], w, b, attrs["eps"])
+    if op == "add_layer_norm":
+        # layer_norm of the sum of the first n_addends operands (the add chain that fed it)
+        k = attrs["n_addends"]
+        w, b = (ops[k], ops[k + 1]) if len(ops) == k + 2 else (None, None)
+        if ops[0].is_cuda:
+            from . import fpkern
+            y = fpkern.add_layer_norm(ops[:k], w, b, attrs["eps"])
+            if y is not None:
+                return y
+        x = ops[0]
+        for t in ops[1:k]:
+            x = x + t
+        return torch.nn.functional.layer_norm(x, attrs["normalized_shape"], w, b, attrs["eps"])
     if op == "reshape":
         return ops[0].reshape(attrs["shape"])
     if op == "cat":

@@ -13,7 +13,7 @@ from __future__ import annotations
 DTYPES = {"f16", "f32"}
 TORCH_OPS = {"add", "mul", "scale", "relu", "exp", "softmax", "matmul", "transpose"}
 # unfused steps the planner emits only with extensions=True (BERT-style blocks)
-EXTENSION_TORCH_OPS = {"gelu", "linear", "layer_norm", "reshape", "permute", "cat", "narrow"}
+EXTENSION_TORCH_OPS = {"gelu", "linear", "layer_norm", "add_layer_norm", "reshape", "permute", "cat", "narrow"}
 LAUNCHES = {"flat", "rows", "attention"}
 _CHAIN_OPS = {"add", "mul", "scale", "relu", "exp", "softmax", "gelu"}
 

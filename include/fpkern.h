@@ -192,6 +192,12 @@ int64_t fpk_chain_jit_launches(void);
 int fpk_layer_norm_fwd(const fpk_ln_desc* d, const void* x, const void* w, const void* b, void* y,
                        void* stream);
 
+/* The same LayerNorm of the sum of n_addends (1..4) inputs, added in f32 in the given
+ * order: bcast[i] is FPK_BCAST_FULL ([rows, cols], contiguous) or FPK_BCAST_COL
+ * (length cols).  The add chain that feeds a LayerNorm (residual + bias), fused into it. */
+int fpk_add_layer_norm_fwd(const fpk_ln_desc* d, const void* const* addends, const int32_t* bcast,
+                           int n_addends, const void* w, const void* b, void* y, void* stream);
+
 /* Synchronise `stream`, then return and clear the device status word of
  * `device` (FPK_OK or the first FPK_ERR_* a kernel recorded, e.g. a timeout). */
 int fpk_poll_status(int device, void* stream);

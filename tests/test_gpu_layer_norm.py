@@ -89,3 +89,42 @@ def test_c_abi_rejects_malformed_descriptors():
     assert lib.fpk_layer_norm_fwd(ctypes.byref(d), ptr, None, None, ptr, stream) == _lib.FPK_ERR_INVALID
     d.eps, d.cols, d.rows = 1e-5, 60, 4
     assert lib.fpk_layer_norm_fwd(ctypes.byref(d), ptr, None, None, ptr, stream) == _lib.FPK_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("shape,dt,kinds", [((16384, 768), torch.float16, ("full", "col", "full")),
+                                            ((9, 1000), torch.float32, ("full", "full")),
+                                            ((5, 2, 64), torch.float16, ("col", "full", "full", "col")),
+                                            ((3, 8), torch.float32, ("full",))])
+def test_add_layer_norm_matches_torch_f32(shape, dt, kinds):
+    """LayerNorm of the in-order sum of full-shape and per-column addends."""
+    g = torch.Generator(device="cuda").manual_seed(len(kinds) + shape[-1])
+    adds = [(torch.randn(shape if k == "full" else shape[-1:], generator=g, device="cuda")).to(dt) for k in kinds]
+    w = (torch.randn(shape[-1], generator=g, device="cuda") * 0.5 + 1).to(dt)
+    b = (torch.randn(shape[-1], generator=g, device="cuda") * 0.1).to(dt)
+    y = fpkern.add_layer_norm(adds, w, b, 1e-5)
+    assert y is not None and tuple(y.shape) == tuple(shape)
+    s = adds[0].float()
+    for t in adds[1:]:
+        s = s + t.float()
+    ref = _ref(s, w, b, 1e-5)
+    atol, rtol = (2e-3, 1e-2) if dt == torch.float16 else (1e-5, 1e-5)
+    torch.testing.assert_close(y.float(), ref, atol=atol, rtol=rtol)
+    assert fpkern.poll_status() == 0
+
+
+def test_add_layer_norm_plan_step_runs_the_kernel(monkeypatch):
+    calls = []
+    real = fpkern.add_layer_norm
+
+    def spy(*a, **k):
+        y = real(*a, **k)
+        calls.append(y is not None)
+        return y
+
+    monkeypatch.setattr(fpkern, "add_layer_norm", spy)
+    a, c = torch.randn(8, 768, device="cuda").half(), torch.randn(8, 768, device="cuda").half()
+    bias, w, b = (torch.randn(768, device="cuda").half() for _ in range(3))
+    step = {"op": "add_layer_norm", "attrs": {"normalized_shape": [768], "eps": 1e-12, "n_addends": 3}}
+    y = runtime._run_torch(step, [a, bias, c, w, b])
+    assert calls == [True]
+    torch.testing.assert_close(y.float(), _ref(a.float() + bias.float() + c.float(), w, b, 1e-12), atol=2e-3, rtol=1e-2)

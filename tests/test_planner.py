@@ -167,8 +167,11 @@ def test_bert_block_plan_shape():
     assert kinds.count("attention") == 1
     chains = [s for s in plan["steps"] if s.get("launch") == "flat"]
     ops = sorted(tuple(o["op"] for o in s["attrs"]["desc"]["ops"]) for s in chains)
-    assert ops == [("add", "add"), ("add", "add"), ("add", "gelu")]
-    assert kinds.count("layer_norm") == 2
+    # the two residual + bias chains feed LayerNorms: fused into add_layer_norm steps
+    assert ops == [("add", "gelu")]
+    lns = [s for s in plan["steps"] if s.get("op") == "add_layer_norm"]
+    assert len(lns) == 2 and kinds.count("layer_norm") == 0
+    assert all(s["attrs"]["n_addends"] == 3 and len(s["operands"]) == 5 for s in lns)
     # the q / k / v biases have no chain to join: folded back into their linear steps, and the
     # three projections of x merged into one GEMM over the concatenated weights and biases
     linears = [s for s in plan["steps"] if s.get("op") == "linear"]
@@ -218,3 +221,33 @@ def test_mlir_text_matches_reference_format():
     assert "fp.transpose %arg1 : tensor<2x4x32x64xf32> -> tensor<2x4x64x32xf32>" in text
     assert "fp.scale" in text and "{factor = 2.500000000e-01 : f32}" in text
     assert "fp.softmax %2 {axis = 3 : i64}" in text
+
+
+def test_add_layer_norm_step_semantics_on_cpu():
+    """The torch form of an add_layer_norm step (used where the kernel does not take the
+    shape): the operands summed in order, then layer_norm."""
+    from fusionpass_b200 import runtime
+    g = torch.Generator().manual_seed(0)
+    a, c = torch.randn(4, 16, generator=g), torch.randn(4, 16, generator=g)
+    bias, w, b = torch.randn(16, generator=g), torch.randn(16, generator=g), torch.randn(16, generator=g)
+    step = {"op": "add_layer_norm", "attrs": {"normalized_shape": [16], "eps": 1e-5, "n_addends": 3}}
+    y = runtime._run_torch(step, [a, bias, c, w, b])
+    ref = torch.nn.functional.layer_norm((a + bias) + c, (16,), w, b, 1e-5)
+    assert torch.equal(y, ref)
+
+
+def test_add_layer_norm_fusion_conditions():
+    class M(nn.Module):
+        def __init__(self, cols):
+            super().__init__()
+            self.lin, self.ln = nn.Linear(cols, cols), nn.LayerNorm(cols)
+
+        def forward(self, x):
+            return self.ln(x + self.lin(x))
+
+    for cols, fused in ((64, True), (20, False), (4096, False)):  # 20 % 8 != 0; above 2048 columns
+        g = planner.trace(M(cols).eval(), (torch.randn(3, cols),), extensions=True)
+        plan, _ = planner.compile_graph(g, fuse=True, extensions=True)
+        kinds = [s.get("op") or s.get("launch") for s in plan["steps"]]
+        assert ("add_layer_norm" in kinds) == fused, (cols, kinds)
+        assert ("layer_norm" in kinds) != fused
