@@ -244,16 +244,20 @@ def layer_norm(x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor 
 
 
 def add_layer_norm(addends, weight: torch.Tensor | None, bias: torch.Tensor | None, eps: float,
-                   out: torch.Tensor | None = None) -> torch.Tensor | None:
+                   out: torch.Tensor | None = None, shape=None) -> torch.Tensor | None:
     """LayerNorm over the last axis of ``addends[0] + addends[1] + ...`` (1 to 4 CUDA
     tensors of the result's shape or vectors of its last dim, summed in f32 in order) in
-    libfpkern.so; None when the kernel does not take the shapes or dtypes."""
+    libfpkern.so; None when the kernel does not take the shapes or dtypes.  ``shape`` is
+    the result's shape (default: that of the addend with the most elements)."""
     ext = extension()
     addends = list(addends)
     if not 1 <= len(addends) <= 4:
         return None
-    full = [t for t in addends if t.dim() >= 1 and t.numel() != t.shape[-1]] or addends[:1]
-    shape = full[0].shape
+    if shape is None:
+        shape = max(addends, key=lambda t: t.numel()).shape
+    shape = tuple(int(d) for d in shape)
+    if not shape:
+        return None
     dt = addends[0].dtype
     for t in addends:
         require_cuda(t, "add_layer_norm")

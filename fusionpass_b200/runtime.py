@@ -58,7 +58,7 @@ def _run_torch(step: dict, ops: list) -> torch.Tensor:
         w, b = (ops[k], ops[k + 1]) if len(ops) == k + 2 else (None, None)
         if ops[0].is_cuda:
             from . import fpkern
-            y = fpkern.add_layer_norm(ops[:k], w, b, attrs["eps"])
+            y = fpkern.add_layer_norm(ops[:k], w, b, attrs["eps"], shape=step.get("shape"))
             if y is not None:
                 return y
         x = ops[0]
