@@ -128,3 +128,13 @@ def test_add_layer_norm_plan_step_runs_the_kernel(monkeypatch):
     y = runtime._run_torch(step, [a, bias, c, w, b])
     assert calls == [True]
     torch.testing.assert_close(y.float(), _ref(a.float() + bias.float() + c.float(), w, b, 1e-12), atol=2e-3, rtol=1e-2)
+
+
+def test_add_layer_norm_single_row_takes_the_step_shape():
+    """A [1, 1, cols] result whose first addend is a per-column vector keeps the step's shape."""
+    g = torch.Generator(device="cuda").manual_seed(2)
+    bias, x = torch.randn(64, generator=g, device="cuda").half(), torch.randn(1, 1, 64, generator=g, device="cuda").half()
+    step = {"op": "add_layer_norm", "shape": [1, 1, 64], "attrs": {"normalized_shape": [64], "eps": 1e-5, "n_addends": 2}}
+    y = runtime._run_torch(step, [bias, x])
+    assert tuple(y.shape) == (1, 1, 64)
+    torch.testing.assert_close(y.float(), _ref(bias.float() + x.float(), None, None, 1e-5), atol=2e-3, rtol=1e-2)
