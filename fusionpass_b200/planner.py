@@ -16,6 +16,13 @@ produced without MLIR:
 * ``fuse_chains``: ``FuseChainPattern`` (``lib/Transforms/FuseChains.cpp:12-90``).
 * ``emit_plan``: ``emitPlan`` (``lib/Plan/PlanEmitter.cpp:59-185``), with each
   fused step carrying its launch descriptor in ``attrs["desc"]``.
+
+Graphs traced with ``extensions=True`` (which the reference cannot trace) get three
+more rewrites after chain fusion, none of which touches the reference's rules:
+``fold_linear_bias`` (a bias add no chain took goes back into its linear step),
+``merge_sibling_linears`` (projections of one input as one GEMM + views) and
+``fuse_add_layer_norm`` (an add chain feeding a LayerNorm, as one step); an
+attention result that only feeds a heads merge is stored in the merged order.
 """
 
 from __future__ import annotations
