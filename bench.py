@@ -519,7 +519,8 @@ def run_configs(args, group: RankGroup, rank: int, world: int, dev) -> dict:
             "fused_steps": {"attention": kinds.count("attention"), "flat_chains": kinds.count("flat")},
             "ms_per_block": round(ms / reps, 4), "value": round(strong_rate(reps, 32 * 512, ms), 1),
             "unit": "tokens/s",
-            "note": "whole block through execute_plan; Linear/LayerNorm run as unfused torch steps"}
+            "note": "whole block through execute_plan: Linear GEMMs in torch (cuBLAS), LayerNorm steps (with the "
+                    "residual adds that feed them) in libfpkern, attention and the bias + GELU chain fused"}
         del m, c, x
 
         # the block's two chain kinds at the block's shapes, each a flat chain over rows
