@@ -35,6 +35,7 @@ struct Params {
   int64_t heads, seq, num_mtiles;
   int64_t qs[3], ks[3], vs[3], os[3];  // b, h, s element strides
   float scale;
+  int vec4;  // k and v bases and strides allow 16-byte loads
 };
 
 // floats of one group's K / V / P buffers
@@ -97,12 +98,38 @@ __global__ void __launch_bounds__(kThreads * G) attn_f32_kernel(const __grid_con
   if constexpr (G > 1) __syncthreads();  // Qs written by every group
   for (int64_t n0 = static_cast<int64_t>(grp) * kBN; n0 < S; n0 += static_cast<int64_t>(G) * kBN) {
     group_sync<G>(grp);  // previous tile fully consumed (and Qs written on the first pass)
-    for (int idx = tid; idx < kBN * D; idx += kThreads) {
-      const int j = idx / D, d = idx % D;
-      const int64_t gj = n0 + j;
-      const bool ok = gj < S;
-      Ks[d][j] = ok ? kb[gj * p.ks[2] + d] : 0.0f;
-      Vs[j][d] = ok ? vb[gj * p.vs[2] + d] : 0.0f;
+    if (p.vec4) {
+      // 16-byte loads, all of a thread's loads issued before any is stored: one memory
+      // latency per key tile instead of one per element
+      constexpr int kPer = kBN * D / 4 / kThreads;  // float4 of K (and of V) per thread
+      float4 kv4[kPer], vv4[kPer];
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int idx = tid + u * kThreads;
+        const int j = idx / (D / 4), d = (idx % (D / 4)) * 4;
+        const int64_t gj = n0 + j;
+        const bool ok = gj < S;
+        kv4[u] = ok ? *reinterpret_cast<const float4*>(kb + gj * p.ks[2] + d) : make_float4(0.f, 0.f, 0.f, 0.f);
+        vv4[u] = ok ? *reinterpret_cast<const float4*>(vb + gj * p.vs[2] + d) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int idx = tid + u * kThreads;
+        const int j = idx / (D / 4), d = (idx % (D / 4)) * 4;
+        Ks[d][j] = kv4[u].x;
+        Ks[d + 1][j] = kv4[u].y;
+        Ks[d + 2][j] = kv4[u].z;
+        Ks[d + 3][j] = kv4[u].w;
+        *reinterpret_cast<float4*>(&Vs[j][d]) = vv4[u];
+      }
+    } else {
+      for (int idx = tid; idx < kBN * D; idx += kThreads) {
+        const int j = idx / D, d = idx % D;
+        const int64_t gj = n0 + j;
+        const bool ok = gj < S;
+        Ks[d][j] = ok ? kb[gj * p.ks[2] + d] : 0.0f;
+        Vs[j][d] = ok ? vb[gj * p.vs[2] + d] : 0.0f;
+      }
     }
     group_sync<G>(grp);
 
@@ -283,11 +310,13 @@ int launch_attention_f32(const fpk_attn_desc* d, const void* q, const void* k, c
   p.heads = d->heads;
   p.seq = d->seq_len;
   p.num_mtiles = 0;  // set by the launch for its tile height
+  p.vec4 = (reinterpret_cast<uintptr_t>(k) % 16 == 0 && reinterpret_cast<uintptr_t>(v) % 16 == 0) ? 1 : 0;
   for (int i = 0; i < 3; ++i) {
     p.qs[i] = d->q_strides[i];
     p.ks[i] = d->k_strides[i];
     p.vs[i] = d->v_strides[i];
     p.os[i] = d->o_strides[i];
+    if (p.ks[i] % 4 || p.vs[i] % 4) p.vec4 = 0;  // every row start stays 16-byte aligned
   }
   p.scale = d->scale;
   const int num_sms = dev.num_sms > 0 ? dev.num_sms : 148;
