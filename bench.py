@@ -56,6 +56,7 @@ RESID_BODY = [{"op": "add", "operands": ["a0", "a1"]}, {"op": "add", "operands":
 L2_BYTES = 126 * 1024 * 1024
 F16_TOL = (2e-3, 1e-2)  # atol, rtol against the reference kernels' results (f16)
 SLEEP_CYCLES = 200_000  # ~0.1 ms of GPU spin before a timed region (see time_graph)
+REF_PASSES = 4  # full CPU passes over the chain workload per step of the reference arm
 
 
 def peaks():
@@ -326,6 +327,21 @@ def chain_oracle(inputs, body, bcast, out_dtype=np.float16):
 
 
 # ----------------------------------------------------------------- CPU legs
+def _keep_freed_memory() -> None:
+    """glibc malloc: serve allocations up to 256 MB from the heap and keep freed memory, so
+    that the numpy temporaries of every oracle pass reuse mapped pages instead of being
+    mapped and faulted in afresh (mallopt M_MMAP_THRESHOLD / M_TRIM_THRESHOLD).  Without it
+    a fresh process ran the CPU passes ~1.7x slower than one whose earlier large
+    allocations had already raised glibc's adaptive threshold.  No-op elsewhere."""
+    try:
+        import ctypes
+        libc = ctypes.CDLL(None)
+        libc.mallopt(-3, 256 << 20)  # M_MMAP_THRESHOLD
+        libc.mallopt(-1, 1 << 30)    # M_TRIM_THRESHOLD
+    except (OSError, AttributeError):
+        pass
+
+
 def oracle_chain_blocks(threads: int):
     """Row blocks of the [4096, 4096] chain workload -- at least one per host thread,
     at most 256 rows each (numpy's temporaries then stay in the allocator's cache
@@ -333,6 +349,7 @@ def oracle_chain_blocks(threads: int):
     restatement of the reference chain kernel) on one block."""
     from oracle import chain as oc
 
+    _keep_freed_memory()
     x, b, s = (t.numpy() for t in chain_inputs())
     ops, res = oc.body_to_program(3, CFG2_BODY)
     rows = min(256, -(-R // max(1, threads)))
@@ -818,25 +835,24 @@ def run_reference(args, world: int):
     """The reference path's CPU implementation -- its chain kernel restated in numpy
     (the oracle port; the reference's own Triton-interpreter path needs its
     checkout, which the GPU box does not have) -- on all host cores, on the same
-    workload, metric and unit: every step is one full pass over the [4096, 4096]
-    chain, split into row blocks over every thread of a single pool."""
+    workload, metric and unit: every step is REF_PASSES full passes over the
+    [4096, 4096] chain (a sample of ~50 ms, so that K steps time a stretch long enough
+    to be steady), split into row blocks over every thread of a single pool."""
     threads = os.cpu_count() or 1
     blocks, task = oracle_chain_blocks(threads)
     with ThreadPoolExecutor(threads) as pool:
-        # W passes, and passes for at least the CPU leg's sample time: a fresh
-        # process runs its first ~30 passes at a third to two thirds of the steady
-        # rate (page faults of numpy's temporaries until the allocator keeps them)
+        # W steps, and passes for at least the CPU leg's sample time, before timing
         t0 = time.perf_counter()
         n = 0
-        while n < args.warmup or time.perf_counter() - t0 < args.cpu_seconds:
+        while n < args.warmup * REF_PASSES or time.perf_counter() - t0 < args.cpu_seconds:
             list(pool.map(task, blocks))
             n += 1
         t0 = time.perf_counter()
-        for _ in range(args.steps):
+        for _ in range(args.steps * REF_PASSES):
             list(pool.map(task, blocks))
         dt = time.perf_counter() - t0
-    gbs = args.steps * CHAIN_BYTES / dt / 1e9
-    sample = (f"every step one full pass over the [4096,4096] chain in {len(blocks)} row blocks on one "
+    gbs = args.steps * REF_PASSES * CHAIN_BYTES / dt / 1e9
+    sample = (f"every step {REF_PASSES} full passes over the [4096,4096] chain in {len(blocks)} row blocks on one "
               f"{threads}-thread pool, numpy oracle port")
     return {
         "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
