@@ -120,6 +120,18 @@ def test_bert_block_compiles_and_verifies():
     assert c.verified, c.report
 
 
+@pytest.mark.parametrize("batch,seq", [(1, 1), (1, 24), (3, 200)])
+def test_bert_block_small_and_ragged_sizes_verify(batch, seq):
+    """The whole rewritten plan (merged projections read as views, attention stored in the
+    heads-merge order, add + LayerNorm, the GELU chain) at one token, a sequence shorter than
+    one key tile and a ragged one, through the equivalence gate."""
+    m = init_bert(BertBlock(batch, seq)).half().to(DEV).eval()
+    x = torch.randn(batch, seq, 768, device=DEV).half()
+    c = compile_model(m, (x,), fuse=True, extensions=True)
+    assert kinds(c).count("add_layer_norm") == 2
+    assert c.verified, c.report
+
+
 def test_gate_catches_miscompile():
     xs = [torch.randn(1, 2, 20, 16, device=DEV) for _ in range(3)]
     c = compile_model(Attn(), xs, fuse=True)
