@@ -235,6 +235,21 @@ def test_attention_f32_vs_oracle(shape):
     _close(out, ref, "f32", f"f32 attention {shape}")
 
 
+def test_attention_f32_scalar_load_path_vs_oracle():
+    """K and V 4-byte but not 16-byte aligned (views one element into their buffers): the
+    kernel falls back from 16-byte to scalar tile loads; same results."""
+    shape = (1, 3, 200, 64)
+    g = torch.Generator().manual_seed(4)
+    q, k, v = (torch.randn(shape, generator=g) for _ in range(3))
+    bufs = [torch.empty(k.numel() + 1, device="cuda") for _ in range(2)]
+    kd, vd = (b[1:].view(shape) for b in bufs)
+    kd.copy_(k)
+    vd.copy_(v)
+    assert kd.data_ptr() % 16 and vd.data_ptr() % 16
+    out = fpkern.attention(q.cuda(), kd, vd, 0.125)
+    _close(out, oracle.attention_fwd(q.numpy(), k.numpy(), v.numpy(), 0.125), "f32", "f32 attention, scalar loads")
+
+
 def test_attention_prefill_config_slices_vs_oracle():
     """B8 H16 S2048 D64 f16 (Q/K/V ~ N(0,1) * D^-1/4, scale 1/8): whole-tensor check
     against a torch f32 reference plus three B*H slices against the oracle."""
