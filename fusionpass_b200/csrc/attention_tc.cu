@@ -19,8 +19,9 @@
 // P has its own columns, Q K^T of key tile j+1 is issued as soon as the softmax
 // has read S_t(j) into registers and runs while the softmax computes P_t(j).
 // One CTA per SM walks its work items; TMEM, the K/V ring and the barrier
-// phases carry across items and O is staged in its own buffer, so an item's
-// epilogue overlaps the next item's first tiles.
+// phases carry across items, Q is double-buffered so the next item's first
+// Q K^T runs during the current item's last key tile, and O is staged in its
+// own buffer, so an item's epilogue overlaps the next item's first tiles.
 //
 // attn_tc_kernel, D = 128 (aliased TMEM layout, one CTA per work item): S_t at
 // 128 t, O_t at 256 + 128 t; P_t overwrites the first 64 columns of S_t.  UMMAs
@@ -743,12 +744,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------- persistent kernel, D <= 64 ---
 // One CTA per SM walks the work items (batch*head, 256-row query block)
 // blockIdx.x, blockIdx.x + gridDim.x, ...  TMEM is allocated once; the K/V ring
-// and every barrier phase run on across items; the next item's Q is loaded as
-// soon as the last Q K^T of the current item has completed, and O is staged in
-// its own buffer, so an item's epilogue overlaps the first tiles of the next.
-// Within an item the schedule is the split-layout one of attn_tc_kernel.
+// and every barrier phase run on across items.  Q is double-buffered by item
+// parity: the next item's Q loads during the current item, and the next item's
+// first Q K^T is issued at the start of the current item's last key iteration,
+// so a softmax warpgroup finds its next S ready when it finishes an item.  O is
+// staged in its own buffer, so an item's epilogue overlaps the first tiles of the
+// next.  Within an item the schedule is the split-layout one of attn_tc_kernel.
 struct PBars {
-  uint64_t q_full, q_empty;
+  uint64_t q_full[2], q_empty[2];  // Q double-buffered by item parity
   uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
   uint64_t s_full[kTiles], p_full[kTiles], o_done[kTiles], s_free[kTiles], turn[kTiles];
   uint64_t epi[kTiles][2];  // the 4 warps of a tile, twice per epilogue (bounded waits)
@@ -783,8 +786,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ PBars bars;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kTiles * C::kTileBytes;
+  uint8_t* sQ = smem;                      // two Q buffers of kTiles tiles (by item parity)
+  uint8_t* sK = sQ + 2 * kTiles * C::kTileBytes;
   uint8_t* sV = sK + NS * C::kTileBytes;
   uint8_t* sO = sV + NS * C::kTileBytes;  // O staging for the TMA store, one tile per softmax warpgroup
 
@@ -805,8 +808,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars.q_full, 1);
-    mbar_init(&bars.q_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars.q_full[b], 1);
+      mbar_init(&bars.q_empty[b], 1);
+    }
     for (int s = 0; s < NS; ++s) {
       mbar_init(&bars.k_full[s], 1);
       mbar_init(&bars.k_empty[s], 1);
@@ -851,13 +856,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int w = blockIdx.x; ok && w < total; w += gridDim.x) {
           int hh, bb, m0, ntiles;
           coords(w, hh, bb, m0, ntiles);
-          // the previous item's Q tiles are free once its last Q K^T has completed
-          if (qn > 0 && !mbar_wait(&bars.q_empty, (qn - 1u) & 1u, abort, p.status, limit)) break;
-          mbar_arrive_expect_tx(&bars.q_full, static_cast<uint32_t>(ntiles * C::kTileBytes));
+          // Q buffer qb is free once the last Q K^T of the item two back has completed
+          const uint32_t qb = qn & 1u;
+          if (qn >= 2u && !mbar_wait(&bars.q_empty[qb], ((qn >> 1) - 1u) & 1u, abort, p.status, limit)) break;
+          mbar_arrive_expect_tx(&bars.q_full[qb], static_cast<uint32_t>(ntiles * C::kTileBytes));
           for (int t = 0; t < ntiles; ++t)
             for (int bx = 0; bx < C::kBoxes; ++bx)
-              tma_load_4d(sQ + t * C::kTileBytes + bx * C::kBoxBytes, &tq, bx * C::kBoxCols, m0 + t * kBM, hh,
-                          bb, &bars.q_full);
+              tma_load_4d(sQ + (qb * kTiles + t) * C::kTileBytes + bx * C::kBoxBytes, &tq, bx * C::kBoxCols,
+                          m0 + t * kBM, hh, bb, &bars.q_full[qb]);
           ++qn;
           for (int j = 0; j < nkv; ++j) {
             if (!mbar_wait(&bars.k_empty[kp], kph ^ 1u, abort, p.status, limit)) {
@@ -889,7 +895,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         // no TMA write may land after the CTA has gone
-        if (qn > 0) drain_wait(&bars.q_full, (qn - 1u) & 1u, p.status);
+        for (uint32_t b = 0; b < 2u; ++b) {
+          const uint32_t loads = (qn + 1u - b) >> 1;  // loads into buffer b
+          if (loads > 0u) drain_wait(&bars.q_full[b], (loads - 1u) & 1u, p.status);
+        }
         for (int s = 0; s < NS; ++s) {
           if (last_k[s] >= 0) drain_wait(&bars.k_full[s], static_cast<uint32_t>(last_k[s]), p.status);
           if (last_v[s] >= 0) drain_wait(&bars.v_full[s], static_cast<uint32_t>(last_v[s]), p.status);
@@ -904,9 +913,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t q_desc = sdesc(smem_u32(sQ), 16, 8 * C::kRowBytes, C::kLayout);
       const uint64_t k_desc = sdesc(smem_u32(sK), 16, 8 * C::kRowBytes, C::kLayout);
       const uint64_t v_desc = sdesc(smem_u32(sV), C::kBoxBytes, 8 * C::kRowBytes, C::kLayout);
-      auto issue_qk = [&](int t, int s) {
+      auto issue_qk = [&](int t, uint32_t qb, int s) {
         const uint32_t d_tmem = tbase + static_cast<uint32_t>(t * 128);
-        const uint64_t a0 = q_desc + static_cast<uint64_t>(t) * kTileStep;
+        const uint64_t a0 = q_desc + static_cast<uint64_t>(qb * kTiles + t) * kTileStep;
         const uint64_t b0 = k_desc + static_cast<uint64_t>(s) * kTileStep;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -927,33 +936,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       int kp = 0, vp = 0;  // ring slot of the next K / V to consume
       uint32_t kph = 0u, vph = 0u;
       uint32_t g0 = 0u, g1 = 0u;  // key iterations done by tile 0 / tile 1 (barrier phases)
-      uint32_t qn = 0u;
+      uint32_t qn = 0u;           // items whose Q buffer has been taken (buffer qn & 1, phase qn >> 1)
+      bool pre = false;           // this item's first Q K^T was issued during the previous item
       bool ok = true;
+      // Q K^T of an item's key tile 0 for tile t from Q buffer qb into S_t, once the
+      // tile's previous S_t (key iteration g - 1, when g > 0) has been read out
+      auto first_qk = [&](int t, uint32_t qb, uint32_t g) -> bool {
+        if (g > 0u && !mbar_wait_w(&bars.s_free[t], (g - 1u) & 1u, abort, p.status, limit)) return false;
+        tc_fence_after();
+        issue_qk(t, qb, kp);
+        mma_commit_l(leader, &bars.s_full[t]);
+        return true;
+      };
       for (int w = blockIdx.x; ok && w < total; w += gridDim.x) {
         int hh, bb, m0, ntiles;
         coords(w, hh, bb, m0, ntiles);
-        if (!mbar_wait_w(&bars.q_full, qn & 1u, abort, p.status, limit) ||
-            !mbar_wait_w(&bars.k_full[kp], kph, abort, p.status, limit))
-          break;
-        ++qn;
-        // S_t is free once the previous item's last S_t has been read out
-        for (int t = 0; t < ntiles; ++t) {
-          const uint32_t g = t == 0 ? g0 : g1;
-          if (g > 0u && !mbar_wait_w(&bars.s_free[t], (g - 1u) & 1u, abort, p.status, limit)) {
-            ok = false;
+        const uint32_t qb = qn & 1u;
+        if (!pre) {
+          if (!mbar_wait_w(&bars.q_full[qb], (qn >> 1) & 1u, abort, p.status, limit) ||
+              !mbar_wait_w(&bars.k_full[kp], kph, abort, p.status, limit))
             break;
+          for (int t = 0; ok && t < ntiles; ++t) ok = first_qk(t, qb, t == 0 ? g0 : g1);
+          if (!ok) break;
+          mma_commit_l(leader, &bars.k_empty[kp]);
+          if (nkv == 1) mma_commit_l(leader, &bars.q_empty[qb]);
+          if (++kp == NS) {
+            kp = 0;
+            kph ^= 1u;
           }
-          tc_fence_after();
-          issue_qk(t, kp);
-          mma_commit_l(leader, &bars.s_full[t]);
         }
-        if (!ok) break;
-        mma_commit_l(leader, &bars.k_empty[kp]);
-        if (nkv == 1) mma_commit_l(leader, &bars.q_empty);
-        if (++kp == NS) {
-          kp = 0;
-          kph ^= 1u;
+        ++qn;
+        // the next item of this CTA: its first Q K^T per tile is issued at the start of
+        // this item's last key iteration (its Q is in the other buffer), before the last
+        // P V, so its S is in TMEM when the softmax finishes this item
+        const int wn = w + static_cast<int>(gridDim.x);
+        int ntn = 0;
+        if (wn < total) {
+          int h2, b2, m2;
+          coords(wn, h2, b2, m2, ntn);
         }
+        pre = false;
         for (int j = 0; ok && j < nkv; ++j) {
           if (j + 1 < nkv) {
             if (!mbar_wait_w(&bars.k_full[kp], kph, abort, p.status, limit)) {
@@ -967,12 +989,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
               }
               tc_fence_after();
-              issue_qk(t, kp);
+              issue_qk(t, qb, kp);
               mma_commit_l(leader, &bars.s_full[t]);
             }
             if (!ok) break;
             mma_commit_l(leader, &bars.k_empty[kp]);
-            if (j + 2 == nkv) mma_commit_l(leader, &bars.q_empty);  // the item's last Q K^T
+            if (j + 2 == nkv) mma_commit_l(leader, &bars.q_empty[qb]);  // the item's last Q K^T
             if (++kp == NS) {
               kp = 0;
               kph ^= 1u;
@@ -981,6 +1003,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait_w(&bars.v_full[vp], vph, abort, p.status, limit)) {
             ok = false;
             break;
+          }
+          const bool early = j + 1 == nkv && ntn > 0;
+          const uint32_t qbn = qb ^ 1u;
+          if (early && (!mbar_wait_w(&bars.q_full[qbn], (qn >> 1) & 1u, abort, p.status, limit) ||
+                        !mbar_wait_w(&bars.k_full[kp], kph, abort, p.status, limit))) {
+            ok = false;
+            break;
+          }
+          if (early) {
+            for (int t = 0; ok && t < ntn; ++t)
+              ok = first_qk(t, qbn, (t == 0 ? g0 : g1) + (t < ntiles ? static_cast<uint32_t>(nkv) : 0u));
+            if (!ok) break;
+            mma_commit_l(leader, &bars.k_empty[kp]);
+            if (nkv == 1) mma_commit_l(leader, &bars.q_empty[qbn]);
+            if (++kp == NS) {
+              kp = 0;
+              kph ^= 1u;
+            }
+            pre = true;
           }
           for (int t = 0; t < ntiles; ++t) {
             const uint32_t g = (t == 0 ? g0 : g1) + static_cast<uint32_t>(j);
@@ -1238,10 +1279,10 @@ static int launch_d(const CUtensorMap* maps, const Params& p, int64_t blocks, cu
   return cudaGetLastError() == cudaSuccess ? FPK_OK : FPK_ERR_CUDA;
 }
 
-// persistent kernel: O staging after the Q tiles and the K / V ring
+// persistent kernel: two Q buffers, the K / V ring, then the O staging tiles
 template <int D>
 constexpr int persistent_smem() {
-  constexpr int bytes = (2 * kTiles + 2 * Cfg<D>::kStages) * Cfg<D>::kTileBytes + 1024;
+  constexpr int bytes = (3 * kTiles + 2 * Cfg<D>::kStages) * Cfg<D>::kTileBytes + 1024;
   return bytes > kMinSmem ? bytes : kMinSmem;
 }
 
