@@ -99,7 +99,8 @@ struct Params {
   int32_t heads;
   int32_t seq;
   int32_t num_mblocks;
-  int32_t num_items;  // batch * heads * num_mblocks (persistent kernel)
+  int32_t num_items;   // work items of the persistent kernel
+  int32_t split_from;  // persistent kernel: items from here on are single 128-row tiles
   float scale_log2;  // scale * log2(e)
   uint32_t flags;
 };
@@ -799,12 +800,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool test_timeout = (p.flags & FPK_FLAG_TEST_TIMEOUT) != 0;
   const uint64_t limit = test_timeout ? kTestWaitLimitNs : kWaitLimitNs;
   volatile int* abort = &bars.abort;
+  // item w: a (batch*head, 256-row block) pair of query tiles, or, from split_from on,
+  // one 128-row half of such a block (items 2i and 2i + 1 past split_from are the two
+  // halves of block split_from + i)
   auto coords = [&](int w, int& hh, int& bb, int& m0, int& ntiles) {
-    const int bh = w / p.num_mblocks;
-    m0 = (w % p.num_mblocks) * (kTiles * kBM);
+    const bool single = w >= p.split_from;
+    const int i = w - p.split_from;
+    const int pw = single ? p.split_from + (i >> 1) : w;
+    const int bh = pw / p.num_mblocks;
+    m0 = (pw % p.num_mblocks) * (kTiles * kBM) + (single ? (i & 1) * kBM : 0);
     hh = bh % p.heads;
     bb = bh / p.heads;
-    ntiles = (m0 + kBM < S) ? 2 : 1;
+    ntiles = (!single && m0 + kBM < S) ? 2 : 1;
   };
 
   if (threadIdx.x == 0) {
@@ -1323,13 +1330,24 @@ int launch_attention_tc(const fpk_attn_desc* d, const void* q, const void* k, co
   p.scale_log2 = d->scale * 1.4426950408889634f;
   p.flags = d->flags;
   const int64_t blocks = d->batch * d->heads * p.num_mblocks;
-  if (blocks > 0x7fffffffLL) return FPK_ERR_UNSUPPORTED;
+  if (blocks > 0x7fffffffLL - 1024) return FPK_ERR_UNSUPPORTED;
   p.num_items = static_cast<int32_t>(blocks);
+  p.split_from = p.num_items;
   const int num_sms = dev.num_sms > 0 ? dev.num_sms : 148;
+  // Persistent kernel: when the last round of 256-row blocks would leave most SMs idle
+  // (at most half of them busy), its blocks run as two single-tile items each, one tile
+  // per SM, so that round takes one tile's time instead of a pair's.  Only when every
+  // block holds two tiles (no empty half).
+  const int64_t rem = blocks % num_sms;
+  const int64_t tail = d->seq_len % (kTiles * kBM);
+  if (blocks > num_sms && rem > 0 && 2 * rem <= num_sms && (tail == 0 || tail > kBM)) {
+    p.split_from = static_cast<int32_t>(blocks - rem);
+    p.num_items = static_cast<int32_t>(blocks + rem);
+  }
   switch (d->head_dim) {
-    case 16: return launch_p<16>(maps, p, blocks, num_sms, stream);
-    case 32: return launch_p<32>(maps, p, blocks, num_sms, stream);
-    case 64: return launch_p<64>(maps, p, blocks, num_sms, stream);
+    case 16: return launch_p<16>(maps, p, p.num_items, num_sms, stream);
+    case 32: return launch_p<32>(maps, p, p.num_items, num_sms, stream);
+    case 64: return launch_p<64>(maps, p, p.num_items, num_sms, stream);
     case 128: return launch_d<128>(maps, p, blocks, stream);
     default: return FPK_ERR_UNSUPPORTED;
   }

@@ -211,6 +211,39 @@ def test_attention_f16_vs_torch_f32(shape):
     _close(out, ref.cpu().numpy(), "f16", f"attention {shape}")
 
 
+def _split_batch(H, S, n_sms):
+    """Smallest batch whose (b*h, 256-row block) items leave a last round of at most half
+    the SMs: the persistent f16 kernel then runs that round's blocks as single 128-row
+    tiles (only when every block holds two tiles: S % 256 == 0 or > 128)."""
+    m = (S + 255) // 256
+    for B in range(1, 64):
+        blocks = B * H * m
+        r = blocks % n_sms
+        if blocks > n_sms and 0 < r and 2 * r <= n_sms:
+            return B, r
+    raise AssertionError("no batch size splits the last round")
+
+
+@pytest.mark.parametrize("H,S,D", [(12, 512, 64), (16, 400, 64), (16, 512, 16), (32, 1024, 32)])
+def test_attention_last_round_split_vs_torch_and_oracle(H, S, D):
+    """Shapes whose last round of work items runs as single-tile items: every row against
+    torch f32, and the last (b, h) slice (all of its blocks in the split round) and the
+    first against the oracle."""
+    n_sms = torch.cuda.get_device_properties(0).multi_processor_count
+    B, r = _split_batch(H, S, n_sms)
+    g = torch.Generator().manual_seed(H + S + D)
+    q, k, v = ((torch.randn(B, H, S, D, generator=g) * D ** -0.25).half() for _ in range(3))
+    scale = D ** -0.5
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    out = fpkern.attention(qc, kc, vc, scale)
+    _close(out, _attn_torch_f32(qc, kc, vc, scale).cpu().numpy(), "f16", f"split B{B} H{H} S{S} D{D} ({r} blocks)")
+    o = out.cpu().numpy().reshape(B * H, S, D)
+    qs, ks, vs = (t.numpy().reshape(B * H, S, D) for t in (q, k, v))
+    for bh in (0, B * H - 1):
+        ref = oracle.attention_fwd(qs[bh:bh + 1], ks[bh:bh + 1], vs[bh:bh + 1], scale)
+        _close(o[bh:bh + 1], ref, "f16", f"split slice {bh}")
+
+
 @pytest.mark.parametrize("scale", [-0.3, 0.0, 2.0])
 def test_attention_f16_unusual_scales(scale):
     g = torch.Generator().manual_seed(11)
