@@ -211,6 +211,20 @@ def test_attention_f16_vs_torch_f32(shape):
     _close(out, ref.cpu().numpy(), "f16", f"attention {shape}")
 
 
+# more (b*h, 256-row block) items than SMs, so every CTA of the persistent f16 kernel walks
+# several and issues the next item's first Q K^T during the current one: items alternating
+# between two tiles and one ((16, 16, 300, 64), (8, 16, 384, 32)), single-tile items of one
+# key tile ((64, 16, 100, 64)), a second tile of one row ((40, 8, 129, 64)), D = 16
+@pytest.mark.parametrize("shape", [(16, 16, 300, 64), (8, 16, 384, 32), (64, 16, 100, 64), (40, 8, 129, 64),
+                                   (20, 16, 200, 16)])
+def test_attention_f16_items_per_cta_vs_torch_f32(shape):
+    g = torch.Generator().manual_seed(sum(shape) + 7)
+    q, k, v = (torch.randn(shape, generator=g).half().cuda() for _ in range(3))
+    scale = shape[-1] ** -0.5
+    out = fpkern.attention(q, k, v, scale)
+    _close(out, _attn_torch_f32(q, k, v, scale).cpu().numpy(), "f16", f"attention {shape}")
+
+
 def _split_batch(H, S, n_sms):
     """Smallest batch whose (b*h, 256-row block) items leave a last round of at most half
     the SMs: the persistent f16 kernel then runs that round's blocks as single 128-row
