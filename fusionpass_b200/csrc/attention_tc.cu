@@ -21,7 +21,10 @@
 // One CTA per SM walks its work items; TMEM, the K/V ring and the barrier
 // phases carry across items, Q is double-buffered so the next item's first
 // Q K^T runs during the current item's last key tile, and O is staged in its
-// own buffer, so an item's epilogue overlaps the next item's first tiles.
+// own buffer, so an item's epilogue overlaps the next item's first tiles.  It
+// is launched as a programmatic dependent launch: its set-up (barriers, TMEM)
+// overlaps the end of the stream's previous kernel, and griddepcontrol.wait
+// holds every global access until that kernel has completed.
 //
 // attn_tc_kernel, D = 128 (aliased TMEM layout, one CTA per work item): S_t at
 // 128 t, O_t at 256 + 128 t; P_t overwrites the first 64 columns of S_t.  UMMAs
@@ -49,6 +52,7 @@
 
 #include <atomic>
 #include <cmath>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -848,6 +852,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = bars.tmem_base;
+  // programmatic dependent launch: the stream's next kernel may be scheduled from now on
+  // (its CTAs find no room on an SM before this kernel's CTA there has exited), and this
+  // kernel touches global memory only once the previous kernel has completed and its
+  // writes are visible
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp >= 2 * kWG / 32) {
     setmaxnreg_dec<kRegsCtl>();
@@ -1305,9 +1315,20 @@ static int launch_p(const CUtensorMap* maps, const Params& p, int64_t items, int
     opted[dev].store(1, std::memory_order_release);
   }
   const int64_t grid = items < num_sms ? items : num_sms;  // one CTA per SM, each walks its items
-  attn_tcp_kernel<D><<<static_cast<unsigned>(grid), kThreads, persistent_smem<D>(), s>>>(maps[0], maps[1], maps[2],
-                                                                                          maps[3], p);
-  return cudaGetLastError() == cudaSuccess ? FPK_OK : FPK_ERR_CUDA;
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = persistent_smem<D>();
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, attn_tcp_kernel<D>, maps[0], maps[1], maps[2], maps[3], p) != cudaSuccess)
+    return FPK_ERR_CUDA;
+  return FPK_OK;
 }
 
 }  // namespace attn_tc

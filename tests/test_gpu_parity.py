@@ -225,6 +225,24 @@ def test_attention_f16_items_per_cta_vs_torch_f32(shape):
     _close(out, _attn_torch_f32(q, k, v, scale).cpu().numpy(), "f16", f"attention {shape}")
 
 
+def test_attention_waits_for_the_kernel_that_wrote_its_inputs():
+    """The persistent f16 kernel is a programmatic dependent launch: a torch kernel that
+    rewrites Q in place right before it (and one that reads O right after) must be ordered
+    with it.  Five rounds with different Q, each checked against torch f32."""
+    B, H, S, D = 4, 16, 1024, 64
+    g = torch.Generator(device="cuda").manual_seed(5)
+    k, v = (torch.randn(B, H, S, D, generator=g, device="cuda").half() for _ in range(2))
+    qs = [torch.randn(B, H, S, D, generator=g, device="cuda").half() for _ in range(5)]
+    q = torch.empty_like(qs[0])
+    outs = []
+    for qi in qs:
+        q.copy_(qi)
+        o = fpkern.attention(q, k, v, 0.125)
+        outs.append(o.float() * 1.0)  # a plain kernel reading O right after
+    for qi, o in zip(qs, outs):
+        _close(o, _attn_torch_f32(qi, k, v, 0.125).cpu().numpy(), "f16", "attention after a producer")
+
+
 def _split_batch(H, S, n_sms):
     """Smallest batch whose (b*h, 256-row block) items leave a last round of at most half
     the SMs: the persistent f16 kernel then runs that round's blocks as single 128-row
