@@ -53,6 +53,7 @@ CFG2_BODY = [{"op": "add", "operands": ["a0", "a1"]}, {"op": "mul", "operands": 
              {"op": "add", "operands": ["t3", "a0"]}]
 GELU_BODY = [{"op": "add", "operands": ["a0", "a1"]}, {"op": "gelu", "operands": ["t0"]}]
 RESID_BODY = [{"op": "add", "operands": ["a0", "a1"]}, {"op": "add", "operands": ["t0", "a2"]}]
+ROWS_BODY = [{"op": "scale", "operands": ["a0"], "factor": 0.5}, {"op": "softmax", "operands": ["t0"]}]
 L2_BYTES = 126 * 1024 * 1024
 F16_TOL = (2e-3, 1e-2)  # atol, rtol against the reference kernels' results (f16)
 SLEEP_CYCLES = 200_000  # ~0.1 ms of GPU spin before a timed region (see time_graph)
@@ -323,7 +324,8 @@ def chain_oracle(inputs, body, bcast, out_dtype=np.float16):
 
     ops, res = oc.body_to_program(len(inputs), body)
     arrs = [t.numpy() for t in inputs]
-    return oc.chain_flat(arrs, ops, res, tuple(inputs[0].shape), out_dtype)
+    run = oc.chain_rows if any(op["op"] == "softmax" for op in body) else oc.chain_flat
+    return run(arrs, ops, res, tuple(inputs[0].shape), out_dtype)
 
 
 # ----------------------------------------------------------------- CPU legs
@@ -427,8 +429,9 @@ def headline_config(world: int) -> dict:
 # ----------------------------------------------------- the other configs
 def run_configs(args, group: RankGroup, rank: int, world: int, dev) -> dict:
     """cfg1 (f32 attention demo), cfg4 (long-sequence D=128 attention), cfg5 (the
-    BERT-base block through the plan executor, and its two chain kinds); each
-    checked before it is timed and strong-scaled over the ranks."""
+    BERT-base block through the plan executor, and its two chain kinds), and the rows
+    form of the chains (softmax at two row lengths); each checked before it is timed
+    and strong-scaled over the ranks."""
     from fusionpass_b200 import fpkern, kernels
 
     from oracle import attention as oa
@@ -545,11 +548,19 @@ def run_configs(args, group: RankGroup, rank: int, world: int, dev) -> dict:
                                      ("cfg5_bias_residual", RESID_BODY, 768, ["full", "col", "full"])):
             out[name] = run_chain_config(name, body, 16384, cols, bc, group, rank, world, dev, stream, pk,
                                          traffic)
+
+    # the rows form of the chains (one last-axis softmax): softmax(x * 0.5) over 67 MB per
+    # launch (x read, y written once) at a short and the longest row it takes
+    if not args.no_rows:
+        for name, rows, cols in (("rows_softmax_4096x4096", 4096, 4096), ("rows_softmax_1024x16384", 1024, 16384)):
+            out[name] = run_chain_config(name, ROWS_BODY, rows, cols, ["full"], group, rank, world, dev, stream, pk,
+                                         traffic)
     return out
 
 
 def run_chain_config(name, body, rows, cols, bcast, group, rank, world, dev, stream, pk, traffic) -> dict:
-    """One flat chain of the BERT block at its full shape, rows split over the ranks."""
+    """One chain at its full shape (a flat chain of the BERT block, or a rows chain with
+    its last-axis softmax), rows split over the ranks."""
     from fusionpass_b200 import fpkern, kernels
 
     desc = kernels.chain_descriptor(len(bcast), body, input_bcast=bcast)
@@ -577,11 +588,19 @@ def run_chain_config(name, body, rows, cols, bcast, group, rank, world, dev, str
     torch.cuda.synchronize(dev)
     ref = chain_oracle(ins, body, bcast)
     y0 = ys[0].cpu()
-    if "gelu" in [op["op"] for op in body]:
+    kinds = [op["op"] for op in body]
+    if "gelu" in kinds:
         frac = budget_frac(y0, torch.from_numpy(ref))
         ok = frac <= 1.0
         chk = (f"whole rank output vs the oracle (f32 erf GELU): {frac:.3f} of the atol 2e-3 / rtol 1e-2 budget "
                "(GELU has no reference kernel)")
+    elif "softmax" in kinds:
+        # softmax outputs are ~1 / cols, far below the f16 atol of 2e-3: a relative check
+        # (the atol only covers the rounding of f16 subnormals)
+        frac = budget_frac(y0, torch.from_numpy(ref), tol=(1e-6, 1e-2))
+        ok = frac <= 1.0
+        chk = (f"whole rank output vs the oracle: {frac:.3f} of an atol 1e-6 / rtol 1e-2 budget (the row "
+               "max, exponentials and sums are not bit-identical to the oracle's)")
     else:
         ok = bool(np.array_equal(y0.numpy(), ref))
         chk = "whole rank output bit-exact vs the oracle"
@@ -590,8 +609,9 @@ def run_chain_config(name, body, rows, cols, bcast, group, rank, world, dev, str
     reps = 50
     ms = time_graph(launch, reps, group, stream)
     gbs = rank_bytes / (ms / reps * 1e-3) / 1e9
-    return {"workload": f"flat chain {' -> '.join(op['op'] for op in body)} over f16 [{rows},{cols}], "
-                        f"per-column bias, seed 0",
+    form = "rows chain" if "softmax" in kinds else "flat chain"
+    extra = ", x ~ N(0,1)" if "softmax" in kinds else ", per-column bias"
+    return {"workload": f"{form} {' -> '.join(op['op'] for op in body)} over f16 [{rows},{cols}]{extra}, seed 0",
             "check": chk, "parallelism": f"rows {nr} per rank over {world} GPU(s) (strong)",
             "launches": reps, "us_per_launch": round(ms / reps * 1e3, 2),
             "value": round(strong_rate(reps, glob_bytes, ms) / 1e9, 1), "unit": "GB/s",
@@ -881,6 +901,7 @@ def main(argv=None) -> int:
     ap.add_argument("--no-configs", action="store_true", help="skip the cfg1/cfg4/cfg5 entries")
     ap.add_argument("--no-long", action="store_true", help="skip the cfg4 entry")
     ap.add_argument("--no-bert", action="store_true", help="skip the cfg5 entries")
+    ap.add_argument("--no-rows", action="store_true", help="skip the rows-chain (softmax) entries")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
