@@ -21,7 +21,9 @@
 // One CTA per SM walks its work items; TMEM, the K/V ring and the barrier
 // phases carry across items, Q is double-buffered so the next item's first
 // Q K^T runs during the current item's last key tile, and O is staged in its
-// own buffer, so an item's epilogue overlaps the next item's first tiles.  It
+// own buffer, so an item's epilogue overlaps the next item's first tiles.  A
+// last round of items that would keep at most half of the SMs busy runs as
+// single-tile items (each 256-row block split in two).  The kernel
 // is launched as a programmatic dependent launch: its set-up (barriers, TMEM)
 // overlaps the end of the stream's previous kernel, and griddepcontrol.wait
 // holds every global access until that kernel has completed.
