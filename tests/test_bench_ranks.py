@@ -87,6 +87,26 @@ def test_shard_range_is_a_contiguous_cover(n, world):
     assert max(sizes) - min(sizes) <= 1
 
 
+def test_rows_chain_gate_uses_the_rows_oracle_and_a_relative_budget():
+    """The bench's rows-chain entries check softmax(x * 0.5) against the oracle's rows
+    restatement; outputs of ~1 / cols sit far below the f16 atol, so the gate is relative:
+    a softmax of the wrong scale passes the f16 budget but fails the relative one."""
+    import numpy as np
+    import torch
+
+    import bench
+
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(4, 4096, generator=g).half()
+    ref = torch.from_numpy(bench.chain_oracle([x], bench.ROWS_BODY, ["full"]))
+    want = torch.softmax(x.float() * 0.5, dim=-1)
+    assert np.allclose(ref.float().numpy(), want.numpy(), rtol=1e-2, atol=1e-6)
+    wrong = torch.softmax(x.float() * 0.4, dim=-1).half()
+    assert bench.budget_frac(wrong, ref) <= 1.0  # the f16 atol of 2e-3 hides it
+    assert bench.budget_frac(wrong, ref, tol=(1e-6, 1e-2)) > 1.0
+    assert bench.budget_frac(ref, ref, tol=(1e-6, 1e-2)) == 0.0
+
+
 def test_rotating_sets_cover_twice_the_l2():
     import bench
 
